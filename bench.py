@@ -1,0 +1,533 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Wan self-attention prep hot path (RMSNorm + 3D RoPE + KV ring write).
+
+Metric: rotated Q/K tokens per second (one token = all heads of Q and K of one position,
+with its V row copied into the ring), whole job, plus the fused kernel's fraction of the
+measured HBM bandwidth.
+
+Default workload ``cfg3`` (Wan2.1-14B same-block batching): 8 streams
+of q, k, v [1560, 40, 128] bf16 ~N(0,1) on a 1x30x52 latent grid, per-stream frame
+offsets drawn from U{3..40}, each stream with a ring of 12 frames written at slot =
+offset mod 12.  One step is one fused launch over the 8-stream batch (one block call);
+successive steps advance every stream by one chunk (offset + 1).  Inputs (384 MB per
+step, two alternating sets) exceed the 126 MB L2, so no flush is needed between steps.
+Under torchrun each rank runs its own 8 streams (weak scaling, no collective on the
+data path).  Other workloads: ``cfg2`` (1.3B, 18 successive chunks per step),
+``cfg4`` (varlen mixed chunks), ``cfg5`` (64 streams sharded over ranks, 30 blocks x 4
+steps per step).
+
+``--impl reference`` times the reference algorithm on the host CPU cores (the oracle's
+restatement of _rope / torch RMSNorm / ring write), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+# --------------------------------------------------------------------------------------
+# Workloads
+# --------------------------------------------------------------------------------------
+WORKLOADS = {
+    "cfg3": dict(model="wan2.1-14b", heads=40, head_dim=128, grid=(1, 30, 52), streams=8, capacity=12,
+                 offsets=(3, 40), launches=1, desc="Wan2.1-14B same-block batch: 8 streams x [1560,40,128] bf16"),
+    "cfg2": dict(model="wan2.1-1.3b", heads=12, head_dim=128, grid=(1, 30, 52), streams=1, capacity=12,
+                 offsets=(3, 3), launches=18, desc="Wan2.1-1.3B steady chunks at offsets 3..20, ring of 12"),
+    "cfg4": dict(model="wan2.2-5b", heads=24, head_dim=128, grid=(1, 22, 40), streams=16, capacity=12,
+                 offsets=(3, 40), launches=1, first_chunks=4,
+                 desc="Wan2.2-5B varlen: 4 first chunks (3x22x40) + 12 steady (1x22x40), H=24"),
+    "cfg5": dict(model="wan2.1-1.3b", heads=12, head_dim=128, grid=(1, 30, 52), streams=64, capacity=12,
+                 offsets=(3, 100), launches=120,
+                 desc="Wan2.1-1.3B 64-stream sweep: 30 blocks x 4 steps per chunk, streams sharded over ranks"),
+}
+
+
+class Workload:
+    """Device buffers and launch list of one rank's share of a workload."""
+
+    def __init__(self, name, rank, world, device, seed=1234):
+        from physisserve_b200.wan import wan_rope_tables
+
+        spec = WORKLOADS[name]
+        self.name, self.spec, self.device = name, spec, device
+        self.heads, self.head_dim = spec["heads"], spec["head_dim"]
+        self.C = self.heads * self.head_dim
+        frames, gh, gw = spec["grid"]
+        self.gh, self.gw, self.hw = gh, gw, gh * gw
+        self.capacity = spec["capacity"]
+        rng = random.Random(seed + 7919 * rank)
+        if name == "cfg5":
+            # Strong scaling: the 64 streams are sharded over ranks (stream i -> rank i % world).
+            self.stream_ids = [i for i in range(spec["streams"]) if i % world == rank]
+        else:
+            self.stream_ids = list(range(spec["streams"]))
+        S = len(self.stream_ids)
+        lo, hi = spec["offsets"]
+        self.offsets = [rng.randint(lo, hi) for _ in range(S)]
+        self.frames = [frames] * S
+        if name == "cfg4":
+            for i in range(spec["first_chunks"]):
+                self.frames[i] = 3
+                self.offsets[i] = 0
+        self.tokens = [f * self.hw for f in self.frames]
+        self.T = sum(self.tokens)
+        self.cu = [0]
+        for t in self.tokens:
+            self.cu.append(self.cu[-1] + t)
+        g = torch.Generator(device="cpu").manual_seed(seed + rank)
+        C, T = self.C, self.T
+        # Input sets rotate per launch; enough of them that a launch never finds its inputs in L2.
+        n_sets = max(2, -(-4 * L2_BYTES // (3 * T * C * 2)))
+        self.inputs = []
+        for _ in range(n_sets):
+            qkv = torch.randn(3, T, C, generator=g).to(torch.bfloat16).to(device)
+            self.inputs.append((qkv[0], qkv[1], qkv[2]))
+        self.n_blocks = 30 if name == "cfg5" else 1
+        self.wq = [(torch.rand(C, generator=g) + 0.5).bfloat16().to(device) for _ in range(self.n_blocks)]
+        self.wk = [(torch.rand(C, generator=g) + 0.5).bfloat16().to(device) for _ in range(self.n_blocks)]
+        max_frame = max(o + f for o, f in zip(self.offsets, self.frames)) + 4096
+        self.cos, self.sin = wan_rope_tables(self.head_dim, max(max_frame, gh, gw), device=device)
+        self.rows = self.capacity * self.hw
+        self.ring_k = torch.zeros(S * self.rows, C, device=device, dtype=torch.bfloat16)
+        self.ring_v = torch.zeros_like(self.ring_k)
+        self.q_out = torch.empty(T, C, device=device, dtype=torch.bfloat16)
+        self.launches_per_step = spec["launches"]
+        self.chunks_per_step = 18 if name == "cfg2" else 1
+        self.tokens_per_launch = T if name != "cfg2" else self.hw
+        self.tokens_per_step = self.tokens_per_launch * self.launches_per_step
+        # Algorithmic HBM bytes: read q, k, v and write q', k'-slot, v-slot (bf16): 12*C per token.
+        self.bytes_per_token = 12 * C
+        self.bytes_per_launch = self.bytes_per_token * self.tokens_per_launch
+
+    def seqs(self, step):
+        from physisserve_b200.ops import Seq
+
+        out = []
+        for i in range(len(self.tokens)):
+            offset = self.offsets[i] + step
+            out.append(Seq(self.cu[i], self.tokens[i], self.gh, self.gw, frame_offset=offset, ring_row=i * self.rows,
+                           ring_frames=self.capacity, ring_slot0=offset % self.capacity))
+        return out
+
+    def run_step(self, step):
+        """Launch one step's kernels on the current stream; returns the number of launches."""
+        from physisserve_b200.ops import Seq, qk_norm_rope_kv
+
+        first = step * self.launches_per_step
+        if self.name == "cfg2":
+            for chunk in range(18):
+                q, k, v = self.inputs[(first + chunk) % len(self.inputs)]
+                offset = 3 + chunk
+                qk_norm_rope_kv(heads=self.heads, head_dim=self.head_dim,
+                                seqs=[Seq(0, self.hw, self.gh, self.gw, offset, 0, 0, self.capacity,
+                                          offset % self.capacity)],
+                                cos=self.cos, sin=self.sin, q=q, k=k, v=v, q_weight=self.wq[0], k_weight=self.wk[0],
+                                eps=1e-6, q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v)
+            return 18
+        seqs = self.seqs(step)
+        n = 0
+        for cell in range(self.launches_per_step):
+            q, k, v = self.inputs[(first + cell) % len(self.inputs)]
+            block = cell % self.n_blocks
+            qk_norm_rope_kv(heads=self.heads, head_dim=self.head_dim, seqs=seqs, cos=self.cos, sin=self.sin, q=q, k=k,
+                            v=v, q_weight=self.wq[block], k_weight=self.wk[block], eps=1e-6, q_out=self.q_out,
+                            k_out=self.ring_k, v_out=self.ring_v)
+            n += 1
+        return n
+
+
+# --------------------------------------------------------------------------------------
+# Clocks
+# --------------------------------------------------------------------------------------
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+            0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """Samples this rank's GPU SM clock, power and clock-event reasons with NVML in a thread."""
+
+    def __init__(self, device_index, period_s=0.002):
+        self.period = period_s
+        self.samples = []
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as exc:  # noqa: BLE001 - NVML is optional on exotic hosts
+            self.error = repr(exc)
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _sample(self):
+        n = self.nvml
+        sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+        try:
+            reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except AttributeError:
+            reasons = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+        power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+        self.samples.append((sm, reasons, power))
+
+    def _loop(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        self._stop.set()
+        self._thread.join()
+        self._sample()
+        sm = [s[0] for s in self.samples]
+        mask = 0
+        for s in self.samples:
+            mask |= s[1]
+        reasons = [name for bit, name in _REASONS.items() if mask & bit]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "power_w_max": max(s[2] for s in self.samples)}
+
+
+# --------------------------------------------------------------------------------------
+# Distributed helpers
+# --------------------------------------------------------------------------------------
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value, world, device):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gather_objects(obj, world):
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+def ncu_traffic(workload):
+    """dram__bytes_read.sum + dram__bytes_write.sum per fused launch from the committed ncu
+    summary (profiles/ncu_traffic.json), scaled to this workload's launch; None if absent."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(workload)
+    return None if entry is None else float(entry["bytes_per_launch"])
+
+
+# --------------------------------------------------------------------------------------
+# CPU reference path (oracle restatement, host cores)
+# --------------------------------------------------------------------------------------
+class CpuReference:
+    """The reference algorithm for one stream chunk on the host CPU: torch RMSNorm of Q and K
+    over H*D, per-token tables sliced from the per-axis tables (WanDiT._frames_table),
+    _rope on Q and K, and the ring write of rotated K and V at slot = offset mod capacity."""
+
+    def __init__(self, spec, seed=99):
+        from oracle import wan_prep as oracle
+
+        self.oracle = oracle
+        self.spec = spec
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        heads, D = spec["heads"], spec["head_dim"]
+        frames, gh, gw = spec["grid"]
+        self.gh, self.gw, self.hw = gh, gw, gh * gw
+        C = heads * D
+        L = frames * self.hw
+        g = torch.Generator().manual_seed(seed)
+        self.q, self.k, self.v = (torch.randn(1, L, C, generator=g).bfloat16() for _ in range(3))
+        self.wq, self.wk = ((torch.rand(C, generator=g) + 0.5).bfloat16() for _ in range(2))
+        self.cos, self.sin = oracle.rope_tables(D, 4096)
+        self.split = oracle.axis_dims(D)
+        self.capacity = spec["capacity"]
+        self.ring_k = torch.zeros(1, self.capacity * self.hw, C, dtype=torch.bfloat16)
+        self.ring_v = torch.zeros_like(self.ring_k)
+        self.tokens = L
+        self.offset = spec["offsets"][0]
+
+    def step(self):
+        o = self.oracle
+        self.offset += 1
+        o.prep_ring(self.q, self.k, self.v, self.wq, self.wk, 1e-6, self.cos, self.sin, self.split, self.gh, self.gw,
+                    [self.offset], self.ring_k, self.ring_v, [self.offset % self.capacity])
+        return self.tokens
+
+    def sample(self, seconds=10.0, min_steps=3):
+        self.step()  # warm
+        steps, tokens = 0, 0
+        t0 = time.perf_counter()
+        while steps < min_steps or time.perf_counter() - t0 < seconds:
+            tokens += self.step()
+            steps += 1
+        elapsed = time.perf_counter() - t0
+        return tokens / elapsed, steps, elapsed
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    spec = WORKLOADS[args.workload]
+    ref = CpuReference(spec)
+    for _ in range(args.warmup):
+        ref.step()
+    t0 = time.perf_counter()
+    tokens = 0
+    for _ in range(args.steps):
+        tokens += ref.step()
+    elapsed = time.perf_counter() - t0
+    value = tokens / elapsed
+    line = {
+        "impl": "reference", "metric": "rotated_qk_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": args.workload, "desc": spec["desc"],
+                   "sample": f"one stream chunk of {ref.tokens} tokens per step (H={spec['heads']}, D=128)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+                         "sample": f"{args.steps} steps x 1 stream chunk ({ref.tokens} tokens)",
+                         "cpu": cpu_model()},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# --------------------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------------------
+def run_ours(args):
+    rank, world, local = init_dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from physisserve_b200 import _lib
+
+    _lib.load()
+    work = Workload(args.workload, rank, world, device)
+    stream = torch.cuda.current_stream(device)
+
+    graph = None
+    if args.graph:
+        # Capture one step; steps then replay it (offsets of step 0).
+        for i in range(2):
+            work.run_step(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            work.run_step(0)
+
+    def step(i):
+        if graph is not None:
+            graph.replay()
+            return work.launches_per_step
+        return work.run_step(i)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+
+    sampler = ClockSampler(local)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    begin.record(stream)
+    launches = 0
+    for i in range(args.steps):
+        starts[i].record(stream)
+        launches += step(args.warmup + i)
+        ends[i].record(stream)
+    finish.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier(world)
+    local_ms = begin.elapsed_time(finish)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = max_over_ranks(local_ms, world, device)
+    tokens_all = sum(gather_objects(work.tokens_per_step * args.steps, world))
+    value = tokens_all / (total_ms / 1000.0)
+
+    # Roofline of the fused kernel: algorithmic bytes per launch / average launch time.
+    launch_ms = sum(step_ms) / (args.steps * work.launches_per_step)
+    achieved = work.bytes_per_launch / (launch_ms / 1000.0) / 1e9
+    peak, peak_src = measured_peak()
+
+    # End to end through the public API: pinned host inputs -> device -> prep -> q' to host.
+    e2e = run_e2e(args, work, world, device, stream)
+
+    all_clocks = gather_objects(clocks, world)
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        ref = CpuReference(WORKLOADS[args.workload])
+        cpu_value, cpu_steps, cpu_s = ref.sample(args.cpu_seconds)
+        cpu = {"value": cpu_value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+               "sample": f"{cpu_steps} stream chunks of {ref.tokens} tokens in {cpu_s:.1f} s", "cpu": cpu_model()}
+
+    if rank == 0:
+        spec = WORKLOADS[args.workload]
+        line = {
+            "metric": "rotated_qk_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong" if args.workload == "cfg5" else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": args.workload, "desc": spec["desc"], "model": spec["model"],
+                       "tokens_per_launch": work.tokens_per_launch, "launches_per_step": work.launches_per_step,
+                       "streams_per_gpu": len(work.tokens), "heads": work.heads, "head_dim": work.head_dim,
+                       "ring_frames": work.capacity, "parallelism": f"streams sharded, dp{world}",
+                       "l2": "inputs larger than L2 (two alternating sets), no flush",
+                       "cuda_graph": bool(graph is not None)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": ncu_traffic(args.workload), "peak_source": peak_src,
+                         "bytes_per_launch": work.bytes_per_launch, "launch_us": launch_ms * 1000.0},
+            "clocks": all_clocks[0] if world == 1 else {"per_rank": all_clocks, **all_clocks[0]},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "cpu_baseline": cpu,
+            "gpu": torch.cuda.get_device_name(device),
+        }
+        print(json.dumps(line))
+    if graph is not None:
+        del graph
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, work, world, device, stream):
+    """The public API end to end: H2D of q, k, v from pinned host memory, the fused prep
+    through physisserve_b200.ops.qk_norm_rope_kv, D2H of the rotated Q (every step)."""
+    from physisserve_b200.ops import qk_norm_rope_kv
+
+    T, C = work.T, work.C
+    host_in = [torch.randn(T, C, generator=torch.Generator().manual_seed(5 + i)).bfloat16().pin_memory()
+               for i in range(3)]
+    host_out = torch.empty(T, C, dtype=torch.bfloat16).pin_memory()
+    dev_in = [torch.empty(T, C, device=device, dtype=torch.bfloat16) for _ in range(3)]
+    steps = max(3, min(args.steps, args.e2e_steps))
+
+    def one(i):
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        qk_norm_rope_kv(heads=work.heads, head_dim=work.head_dim, seqs=work.seqs(i), cos=work.cos, sin=work.sin,
+                        q=dev_in[0], k=dev_in[1], v=dev_in[2], q_weight=work.wq[0], k_weight=work.wk[0], eps=1e-6,
+                        q_out=work.q_out, k_out=work.ring_k, v_out=work.ring_v)
+        host_out.copy_(work.q_out, non_blocking=True)
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record(stream)
+    for i in range(steps):
+        one(i)
+    finish.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(begin.elapsed_time(finish), world, device)
+    tokens = T * steps * world
+    return {"value": tokens / (ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": 3 * T * C * 2,
+            "d2h_bytes_per_step": T * C * 2, "steps": steps, "api": "physisserve_b200.ops.qk_norm_rope_kv"}
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3")
+    parser.add_argument("--graph", action="store_true", help="replay each step from a captured CUDA graph")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--e2e-steps", type=int, default=20)
+    args = parser.parse_args(argv)
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

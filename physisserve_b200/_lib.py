@@ -1,0 +1,131 @@
+"""ctypes binding of ``libphysis_b200.so`` (declared in ``include/physis_b200.h``).
+
+The library is loaded from ``physisserve_b200/lib/`` only.  There is no fallback:
+if the shared library is missing, importing the ops raises, so a GPU host can never
+silently run a non-native path.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libphysis_b200.so"
+
+ABI_VERSION = 1
+MAX_SEQS = 64
+
+# ps_status
+OK, ERR_NULL, ERR_SHAPE, ERR_ALIGN, ERR_BOUNDS, ERR_DTYPE, ERR_UNSUPPORTED, ERR_LAUNCH, ERR_TOO_MANY_SEQS = range(9)
+STATUS_NAMES = {
+    OK: "PS_OK", ERR_NULL: "PS_ERR_NULL", ERR_SHAPE: "PS_ERR_SHAPE", ERR_ALIGN: "PS_ERR_ALIGN",
+    ERR_BOUNDS: "PS_ERR_BOUNDS", ERR_DTYPE: "PS_ERR_DTYPE", ERR_UNSUPPORTED: "PS_ERR_UNSUPPORTED",
+    ERR_LAUNCH: "PS_ERR_LAUNCH", ERR_TOO_MANY_SEQS: "PS_ERR_TOO_MANY_SEQS",
+}
+# ps_dtype
+BF16, F32 = 0, 1
+# ps_table_mode
+TABLE_TOKENS, TABLE_AXES = 0, 1
+
+EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
+           "ps_rope", "ps_rope_validate")
+
+
+class PsSeq(ctypes.Structure):
+    """``ps_seq``: one stream chunk / batch member / varlen member."""
+
+    _fields_ = [
+        ("token_start", ctypes.c_int64),
+        ("n_tokens", ctypes.c_int32),
+        ("grid_h", ctypes.c_int32),
+        ("grid_w", ctypes.c_int32),
+        ("frame_offset", ctypes.c_int32),
+        ("table_row", ctypes.c_int64),
+        ("ring_row", ctypes.c_int64),
+        ("ring_frames", ctypes.c_int32),
+        ("ring_slot0", ctypes.c_int32),
+    ]
+
+
+class PsQkPrepArgs(ctypes.Structure):
+    """``ps_qk_prep_args``."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("table_mode", ctypes.c_int32),
+        ("t_dim", ctypes.c_int32),
+        ("h_dim", ctypes.c_int32),
+        ("w_dim", ctypes.c_int32),
+        ("n_seqs", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("heads_per_thread", ctypes.c_int32),
+        ("in_rows", ctypes.c_int64),
+        ("q", ctypes.c_void_p), ("q_stride", ctypes.c_int64),
+        ("k", ctypes.c_void_p), ("k_stride", ctypes.c_int64),
+        ("v", ctypes.c_void_p), ("v_stride", ctypes.c_int64),
+        ("q_weight", ctypes.c_void_p),
+        ("k_weight", ctypes.c_void_p),
+        ("cos", ctypes.c_void_p),
+        ("sin", ctypes.c_void_p),
+        ("table_rows", ctypes.c_int64),
+        ("q_out", ctypes.c_void_p), ("q_out_stride", ctypes.c_int64),
+        ("k_out", ctypes.c_void_p), ("k_out_stride", ctypes.c_int64),
+        ("v_out", ctypes.c_void_p), ("v_out_stride", ctypes.c_int64),
+        ("kv_out_rows", ctypes.c_int64),
+        ("k_pre", ctypes.c_void_p), ("k_pre_stride", ctypes.c_int64),
+        ("seqs", ctypes.POINTER(PsSeq)),
+    ]
+
+
+class NativeError(RuntimeError):
+    """A non-zero ``ps_status`` from the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+_LIB = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library once (raises if it was not built)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m physisserve_b200.build`")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    lib.ps_abi_version.restype = ctypes.c_int32
+    lib.ps_abi_version.argtypes = []
+    lib.ps_error_message.restype = ctypes.c_char_p
+    lib.ps_error_message.argtypes = []
+    lib.ps_qk_prep_validate.restype = ctypes.c_int32
+    lib.ps_qk_prep_validate.argtypes = [ctypes.POINTER(PsQkPrepArgs)]
+    lib.ps_qk_norm_rope_kv.restype = ctypes.c_int32
+    lib.ps_qk_norm_rope_kv.argtypes = [ctypes.POINTER(PsQkPrepArgs), ctypes.c_void_p]
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    rope_args = [ctypes.c_int32, ctypes.c_void_p, i64p, ctypes.c_void_p, ctypes.c_void_p, i64p, ctypes.c_void_p,
+                 i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]
+    lib.ps_rope.restype = ctypes.c_int32
+    lib.ps_rope.argtypes = [*rope_args, ctypes.c_void_p]
+    lib.ps_rope_validate.restype = ctypes.c_int32
+    lib.ps_rope_validate.argtypes = rope_args
+    version = lib.ps_abi_version()
+    if version != ABI_VERSION:
+        raise ImportError(f"{LIB_PATH} has ABI version {version}, expected {ABI_VERSION}")
+    _LIB = lib
+    return lib
+
+
+def check(status: int) -> None:
+    """Raise ``NativeError`` (a ValueError-like failure) for a non-zero status."""
+    if status != OK:
+        message = load().ps_error_message().decode(errors="replace")
+        raise NativeError(status, message)
+
+
+def int64_array(values) -> ctypes.Array:
+    values = [int(v) for v in values]
+    return (ctypes.c_int64 * len(values))(*values)

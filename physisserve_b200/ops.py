@@ -1,0 +1,245 @@
+"""Torch-facing wrappers of the native sm_100a kernels (``include/physis_b200.h``).
+
+Tensors are passed to the C ABI as raw device pointers plus element strides; every
+launch goes on the current CUDA stream of the tensors' device.  These wrappers
+allocate only the outputs the reference also allocates (``torch.empty_like`` in
+``_rope``, wan.py:60); all validation errors surface as ``ValueError``
+(``NativeError``) carrying the library's message.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+
+class PrepError(ValueError):
+    """Invalid arguments for a prep kernel (mirrors the reference's ValueError checks)."""
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise PrepError(f"unsupported dtype {t.dtype}: the kernels take bfloat16 or float32") from None
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check(status: int) -> None:
+    if status != _lib.OK:
+        message = _lib.load().ps_error_message().decode(errors="replace")
+        raise PrepError(f"{_lib.STATUS_NAMES.get(status, status)}: {message}")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise PrepError("the prep kernels run on CUDA tensors only (there is no CPU path)")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise PrepError(f"tensors on different devices: {device} and {t.device}")
+    return device
+
+
+# --------------------------------------------------------------------------------------
+# _rope drop-in
+# --------------------------------------------------------------------------------------
+def rope(x: torch.Tensor, cosine: torch.Tensor, sine: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Drop-in for the reference's ``_rope(x, cosine, sine)`` (wan.py:58-63).
+
+    ``x``: [B, L, H, D] (any strides with a unit D stride), bfloat16 or float32.
+    ``cosine``/``sine``: float32 [B or 1, L, 1, D].  Returns ``torch.empty_like(x)``
+    filled with the rotated values (same dtype and strides as ``x``), or writes ``out``.
+    """
+    if x.dim() != 4:
+        raise PrepError(f"x must be [B, L, H, D], got {tuple(x.shape)}")
+    B, L, H, D = x.shape
+    for name, t in (("cosine", cosine), ("sine", sine)):
+        if t.dtype != torch.float32:
+            raise PrepError(f"{name} must be float32 (the reference's tables are fp32)")
+        if t.dim() != 4 or t.shape[1] != L or t.shape[2] != 1 or t.shape[3] != D or t.shape[0] not in (1, B):
+            raise PrepError(f"{name} must be [B or 1, {L}, 1, {D}], got {tuple(t.shape)}")
+    if cosine.stride() != sine.stride():
+        sine = sine.contiguous() if sine.stride() != cosine.contiguous().stride() else sine
+        cosine = cosine.contiguous()
+    if cosine.stride(3) != 1:
+        cosine, sine = cosine.contiguous(), sine.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    elif out.shape != x.shape or out.dtype != x.dtype:
+        raise PrepError("out must match x in shape and dtype")
+    device = _require_cuda(x, cosine, sine, out)
+    if x.stride(3) != 1 or out.stride(3) != 1:
+        raise PrepError("x and out need a unit stride on the head dimension")
+    tab_batch = 0 if cosine.shape[0] == 1 else cosine.stride(0)
+    lib = _lib.load()
+    status = lib.ps_rope(_dtype_code(x), ctypes.c_void_p(x.data_ptr()), _lib.int64_array(x.stride()[:3]),
+                         ctypes.c_void_p(cosine.data_ptr()), ctypes.c_void_p(sine.data_ptr()),
+                         _lib.int64_array((tab_batch, cosine.stride(1))), ctypes.c_void_p(out.data_ptr()),
+                         _lib.int64_array(out.stride()[:3]), B, L, H, D, _stream(device))
+    _check(status)
+    return out
+
+
+# --------------------------------------------------------------------------------------
+# Fused RMSNorm + RoPE + ring write
+# --------------------------------------------------------------------------------------
+@dataclass
+class Seq:
+    """One sequence of a fused call (``ps_seq``).
+
+    ``token_start``/``n_tokens``: its rows in q/k/v; ``grid_h``/``grid_w``: latent grid per
+    frame; ``frame_offset``: absolute latent frame of its first frame (per-axis tables);
+    ``table_row``: table row of its first token (per-token tables); ``ring_row``,
+    ``ring_frames``, ``ring_slot0``: where frame f's K/V rows go -- slot
+    (ring_slot0 + f) % ring_frames of the ring starting at row ``ring_row``.
+    """
+
+    token_start: int
+    n_tokens: int
+    grid_h: int
+    grid_w: int
+    frame_offset: int = 0
+    table_row: int = 0
+    ring_row: int = 0
+    ring_frames: int = 0
+    ring_slot0: int = 0
+
+    def to_c(self) -> _lib.PsSeq:
+        return _lib.PsSeq(self.token_start, self.n_tokens, self.grid_h, self.grid_w, self.frame_offset,
+                          self.table_row, self.ring_row, self.ring_frames, self.ring_slot0)
+
+
+def flat_seq(token_start: int, n_tokens: int, grid_h: int, grid_w: int, frame_offset: int = 0,
+             table_row: int = 0) -> Seq:
+    """A sequence whose K/V output rows mirror its input rows (no ring)."""
+    frames = max(1, n_tokens // (grid_h * grid_w))
+    return Seq(token_start, n_tokens, grid_h, grid_w, frame_offset, table_row, token_start, frames, 0)
+
+
+def _rows(t: torch.Tensor | None, C: int, name: str):
+    """(pointer, row stride, rows) of a token-major [..., C] or [..., H, D] tensor."""
+    if t is None:
+        return None, 0, 0
+    if t.dim() >= 2 and t.shape[-1] * t.shape[-2] == C and t.shape[-1] != C:
+        if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
+            raise PrepError(f"{name}: heads of a token must be contiguous")
+        t = t.flatten(-2)
+    if t.shape[-1] != C or t.stride(-1) != 1:
+        raise PrepError(f"{name}: last dimension must be C={C} with unit stride, got {tuple(t.shape)}")
+    try:
+        rows = t.view(-1, C) if t.dim() != 2 else t
+    except RuntimeError:
+        raise PrepError(f"{name}: leading dimensions must collapse to one row dimension (token-major layout)") from None
+    return rows.data_ptr(), rows.stride(0), rows.shape[0]
+
+
+def qk_norm_rope_kv(
+    *,
+    heads: int,
+    head_dim: int,
+    seqs: Sequence[Seq],
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    q: torch.Tensor | None = None,
+    k: torch.Tensor | None = None,
+    v: torch.Tensor | None = None,
+    q_weight: torch.Tensor | None = None,
+    k_weight: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    q_out: torch.Tensor | None = None,
+    k_out: torch.Tensor | None = None,
+    v_out: torch.Tensor | None = None,
+    k_pre: torch.Tensor | None = None,
+    table_mode: str = "axes",
+    axis_split: Sequence[int] | None = None,
+    heads_per_thread: int = 0,
+) -> None:
+    """One fused launch (per ``PS_MAX_SEQS`` sequences) of ``ps_qk_norm_rope_kv``.
+
+    Replaces norm_q/norm_k (wan.py:104-105), the K/V write of ``Cache`` (kv_cache.py:51-56)
+    and ``_rope`` of Q and of the chunk's K (wan.py:108-109).  ``table_mode`` is "axes"
+    (``cos``/``sin`` are the [max_len, D] per-axis tables, positions decoded from each
+    sequence's grid and frame offset) or "tokens" (``cos``/``sin`` are per-token rows,
+    [rows, D] or the reference's [B, L, 1, D] tables, read at ``table_row + l``).
+    """
+    C = heads * head_dim
+    ref = next(t for t in (q, k, v) if t is not None)
+    device = _require_cuda(q, k, v, q_weight, k_weight, cos, sin, q_out, k_out, v_out, k_pre)
+    dtype = _dtype_code(ref)
+    for name, t in (("q", q), ("k", k), ("v", v), ("q_out", q_out), ("k_out", k_out), ("v_out", v_out),
+                    ("k_pre", k_pre), ("q_weight", q_weight), ("k_weight", k_weight)):
+        if t is not None and t.dtype != ref.dtype:
+            raise PrepError(f"{name} is {t.dtype}, expected {ref.dtype}")
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.dtype != torch.float32:
+            raise PrepError(f"{name} must be float32")
+        if t.shape[-1] != head_dim or not t.is_contiguous():
+            raise PrepError(f"{name} must be contiguous with last dimension head_dim={head_dim}")
+    if cos.shape != sin.shape:
+        raise PrepError("cos and sin differ in shape")
+    mode = {"axes": _lib.TABLE_AXES, "tokens": _lib.TABLE_TOKENS}[table_mode]
+    if mode == _lib.TABLE_AXES:
+        split = tuple(axis_split) if axis_split is not None else _default_split(head_dim)
+    else:
+        split = (0, 0, 0)
+    for name, w in (("q_weight", q_weight), ("k_weight", k_weight)):
+        if w is not None and (w.numel() != C or not w.is_contiguous()):
+            raise PrepError(f"{name} must be a contiguous [{C}] vector")
+
+    qp, qs, q_rows = _rows(q, C, "q")
+    kp, ks, k_rows = _rows(k, C, "k")
+    vp, vs, v_rows = _rows(v, C, "v")
+    qop, qos, qo_rows = _rows(q_out, C, "q_out")
+    kop, kos, ko_rows = _rows(k_out, C, "k_out")
+    vop, vos, vo_rows = _rows(v_out, C, "v_out")
+    kpp, kps, kp_rows = _rows(k_pre, C, "k_pre")
+    in_rows = min(r for r, t in ((q_rows, q), (k_rows, k), (v_rows, v), (qo_rows, q_out), (kp_rows, k_pre))
+                  if t is not None)
+    kv_rows = min([r for r, t in ((ko_rows, k_out), (vo_rows, v_out)) if t is not None] or [0])
+    table_rows = cos.numel() // head_dim
+
+    lib = _lib.load()
+    stream = _stream(device)
+    seqs = list(seqs)
+    for begin in range(0, max(1, len(seqs)), _lib.MAX_SEQS):
+        part = seqs[begin:begin + _lib.MAX_SEQS]
+        array = (_lib.PsSeq * len(part))(*[s.to_c() for s in part])
+        args = _lib.PsQkPrepArgs(
+            dtype=dtype, heads=heads, head_dim=head_dim, table_mode=mode,
+            t_dim=split[0], h_dim=split[1], w_dim=split[2], n_seqs=len(part), eps=float(eps),
+            heads_per_thread=heads_per_thread, in_rows=in_rows,
+            q=qp, q_stride=qs, k=kp, k_stride=ks, v=vp, v_stride=vs,
+            q_weight=None if q_weight is None else q_weight.data_ptr(),
+            k_weight=None if k_weight is None else k_weight.data_ptr(),
+            cos=cos.data_ptr(), sin=sin.data_ptr(), table_rows=table_rows,
+            q_out=qop, q_out_stride=qos, k_out=kop, k_out_stride=kos, v_out=vop, v_out_stride=vos,
+            kv_out_rows=kv_rows, k_pre=kpp, k_pre_stride=kps,
+            seqs=ctypes.cast(array, ctypes.POINTER(_lib.PsSeq)))
+        _check(lib.ps_qk_norm_rope_kv(ctypes.byref(args), stream))
+
+
+def _default_split(head_dim: int) -> tuple[int, int, int]:
+    """Wan's split of the head dim into frame / row / column columns: h = w = 2*(D//6)."""
+    h = w = 2 * (head_dim // 6)
+    return head_dim - h - w, h, w
+
+
+def ring_slot(frame_offset: int, capacity: int, origin: int = 0) -> int:
+    """Ring slot of absolute latent frame ``frame_offset``: (frame_offset - origin) mod capacity."""
+    if capacity <= 0:
+        raise PrepError("ring capacity must be positive")
+    return (frame_offset - origin) % capacity

@@ -1,0 +1,162 @@
+"""The C ABI without a GPU: the library loads, exports every declared symbol, its
+struct layouts match the header, and host-side validation returns the documented
+status codes (no CUDA call is made by ps_*_validate)."""
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from physisserve_b200 import _lib
+from physisserve_b200.build import INCLUDE, build
+
+HEADER = INCLUDE / "physis_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return re.findall(r"PS_API\s+[\w\s\*]+?\b(ps_\w+)\s*\(", text)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert set(names) == set(_lib.EXPORTS)
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    for name in names:
+        assert name in exported, name
+        assert hasattr(lib, name)
+
+
+def test_abi_version(lib):
+    assert lib.ps_abi_version() == _lib.ABI_VERSION
+
+
+def test_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text("""
+#include <stdio.h>
+#include <stddef.h>
+#include "physis_b200.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu\\n", sizeof(ps_seq), offsetof(ps_seq, table_row), offsetof(ps_seq, ring_slot0),
+         sizeof(ps_qk_prep_args), offsetof(ps_qk_prep_args, seqs));
+  printf("%zu %zu %zu\\n", offsetof(ps_qk_prep_args, in_rows), offsetof(ps_qk_prep_args, cos),
+         offsetof(ps_qk_prep_args, k_pre_stride));
+  return 0;
+}
+""")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(INCLUDE), str(src), "-o", str(exe)], check=True)
+    line1, line2 = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")[:2]
+    want1 = [ctypes.sizeof(_lib.PsSeq), _lib.PsSeq.table_row.offset, _lib.PsSeq.ring_slot0.offset,
+             ctypes.sizeof(_lib.PsQkPrepArgs), _lib.PsQkPrepArgs.seqs.offset]
+    want2 = [_lib.PsQkPrepArgs.in_rows.offset, _lib.PsQkPrepArgs.cos.offset, _lib.PsQkPrepArgs.k_pre_stride.offset]
+    assert [int(x) for x in line1.split()] == want1
+    assert [int(x) for x in line2.split()] == want2
+
+
+# ---------------------------------------------------------------------------------------
+# Host-side validation (fake, never dereferenced, 16-byte aligned addresses)
+# ---------------------------------------------------------------------------------------
+BASE = 1 << 40
+
+
+def _args(**over):
+    H, D = over.pop("heads", 12), over.pop("head_dim", 128)
+    C = H * D
+    L = over.pop("tokens", 1560)
+    seqs = over.pop("seqs", [_lib.PsSeq(0, L, 30, 52, 3, 0, 0, 12, 3)])
+    array = (_lib.PsSeq * len(seqs))(*seqs)
+    fields = dict(dtype=_lib.BF16, heads=H, head_dim=D, table_mode=_lib.TABLE_AXES, t_dim=44, h_dim=42, w_dim=42,
+                  n_seqs=len(seqs), eps=1e-6, heads_per_thread=0, in_rows=L,
+                  q=BASE, q_stride=C, k=BASE + 0x10000000, k_stride=C, v=BASE + 0x20000000, v_stride=C,
+                  q_weight=BASE + 0x30000000, k_weight=BASE + 0x30100000,
+                  cos=BASE + 0x40000000, sin=BASE + 0x41000000, table_rows=1024,
+                  q_out=BASE + 0x50000000, q_out_stride=C, k_out=BASE + 0x60000000, k_out_stride=C,
+                  v_out=BASE + 0x70000000, v_out_stride=C, kv_out_rows=12 * 1560, k_pre=None, k_pre_stride=0)
+    fields.update(over)
+    args = _lib.PsQkPrepArgs(**fields, seqs=ctypes.cast(array, ctypes.POINTER(_lib.PsSeq)))
+    args._keep = array
+    return args
+
+
+def _validate(lib, args):
+    status = lib.ps_qk_prep_validate(ctypes.byref(args))
+    return status, lib.ps_error_message().decode()
+
+
+def test_validate_accepts_config2(lib):
+    assert _validate(lib, _args()) == (_lib.OK, "")
+
+
+@pytest.mark.parametrize("over,status,text", [
+    (dict(dtype=7), _lib.ERR_DTYPE, "dtype"),
+    (dict(q=BASE + 8), _lib.ERR_ALIGN, "q is not 16-byte aligned"),
+    (dict(q_stride=1537), _lib.ERR_ALIGN, "row stride"),
+    (dict(q_stride=100), _lib.ERR_SHAPE, "below C"),
+    (dict(cos=None), _lib.ERR_NULL, "cos"),
+    (dict(t_dim=43, h_dim=43), _lib.ERR_SHAPE, "axis split"),
+    (dict(t_dim=40), _lib.ERR_SHAPE, "axis split"),
+    (dict(head_dim=100, heads=12), _lib.ERR_ALIGN, "16-byte vectors"),
+    (dict(table_rows=20), _lib.ERR_BOUNDS, "exceed table_rows"),
+    (dict(kv_out_rows=12 * 1560 - 1), _lib.ERR_BOUNDS, "kv_out_rows"),
+    (dict(in_rows=1000), _lib.ERR_BOUNDS, "in_rows"),
+    (dict(q=None, k=None, v=None), _lib.ERR_NULL, "all NULL"),
+    (dict(k_out=None), _lib.ERR_NULL, "k given without k_out or k_pre"),
+    (dict(heads_per_thread=5), _lib.ERR_UNSUPPORTED, "does not divide"),
+    (dict(heads_per_thread=7, heads=7, seqs=[_lib.PsSeq(0, 1560, 30, 52, 3, 0, 0, 12, 3)]), _lib.ERR_UNSUPPORTED,
+     "not compiled"),
+])
+def test_validate_rejects(lib, over, status, text):
+    got, message = _validate(lib, _args(**over))
+    assert got == status, message
+    assert text in message
+
+
+@pytest.mark.parametrize("seq,text", [
+    (_lib.PsSeq(0, 1561, 30, 52, 3, 0, 0, 12, 3), "whole frames"),
+    (_lib.PsSeq(0, 1560, 30, 52, 3, 0, 0, 12, 12), "ring slot"),
+    (_lib.PsSeq(0, 1560, 30, 52, 3, 0, 0, 0, 0), "ring slot"),
+    (_lib.PsSeq(0, 1560, 30, 52, -1, 0, 0, 12, 0), "exceed table_rows"),
+    (_lib.PsSeq(0, 4680, 30, 52, 0, 0, 0, 2, 0), "overwrite each other"),
+    (_lib.PsSeq(-1, 1560, 30, 52, 3, 0, 0, 12, 0), "outside in_rows"),
+])
+def test_validate_rejects_sequences(lib, seq, text):
+    got, message = _validate(lib, _args(seqs=[seq], in_rows=4680, kv_out_rows=100000))
+    assert got != _lib.OK
+    assert text in message
+
+
+def test_validate_too_many_sequences(lib):
+    seqs = [_lib.PsSeq(0, 0, 1, 1, 0, 0, 0, 1, 0)] * (_lib.MAX_SEQS + 1)
+    got, message = _validate(lib, _args(seqs=seqs))
+    assert got == _lib.ERR_TOO_MANY_SEQS
+
+
+def test_validate_token_table_mode(lib):
+    args = _args(table_mode=_lib.TABLE_TOKENS, table_rows=1560,
+                 seqs=[_lib.PsSeq(0, 1560, 1, 1560, 0, 0, 0, 12, 3)])
+    assert _validate(lib, args)[0] == _lib.OK
+    args = _args(table_mode=_lib.TABLE_TOKENS, table_rows=1559,
+                 seqs=[_lib.PsSeq(0, 1560, 1, 1560, 0, 0, 0, 12, 3)])
+    assert _validate(lib, args)[0] == _lib.ERR_BOUNDS
+
+
+def test_rope_validate(lib):
+    strides = _lib.int64_array([1560 * 12 * 128, 12 * 128, 128])
+    tab = _lib.int64_array([0, 128])
+    ok = lib.ps_rope_validate(_lib.BF16, BASE, strides, BASE + 0x1000000, BASE + 0x2000000, tab, BASE + 0x3000000,
+                              strides, 1, 1560, 12, 128)
+    assert ok == _lib.OK
+    bad = lib.ps_rope_validate(_lib.BF16, BASE + 2, strides, BASE, BASE, tab, BASE, strides, 1, 1560, 12, 128)
+    assert bad == _lib.ERR_ALIGN
+    odd = lib.ps_rope_validate(_lib.BF16, BASE, strides, BASE, BASE, tab, BASE, strides, 1, 1560, 12, 7)
+    assert odd == _lib.ERR_SHAPE

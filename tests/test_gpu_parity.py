@@ -1,0 +1,431 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the CPU oracle and with the
+golden vectors recorded from the reference.  Tolerances are stated in tests/helpers.py."""
+import random
+
+import pytest
+import torch
+
+from oracle import wan_prep as oracle
+from physisserve_b200 import ops
+from physisserve_b200.ops import Seq, qk_norm_rope_kv
+from physisserve_b200.wan import Attention, RingCache, prep_ring, prepare_reference_layout, rope, window_layout
+
+from helpers import (check_against_exact, check_bf16_close, exact_prep, norm_weight, pair_magnitude, randn,
+                      token_tables)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+EPS = 1e-6
+
+
+# ---------------------------------------------------------------------------------------
+# _rope drop-in: bit-exact against the reference's own outputs
+# ---------------------------------------------------------------------------------------
+def test_rope_bit_exact_against_reference_vectors(golden):
+    for case in golden("rope_cases.pt"):
+        cos, sin = case["cos"].to(DEV), case["sin"].to(DEV)
+        if "x_storage" in case:
+            storage = case["x_storage"].to(DEV)
+            got = rope(storage.transpose(1, 2), cos, sin).transpose(1, 2)
+            assert got.is_contiguous()
+        else:
+            x = case["x"].to(DEV)
+            got = rope(x, cos, sin)
+            assert got.stride() == x.stride()
+        assert torch.equal(got.cpu(), case["out"]), case["name"]
+
+
+def test_rope_in_place_and_out_argument(golden):
+    case = golden("rope_cases.pt")[0]
+    x = case["x"].to(DEV)
+    out = torch.empty_like(x)
+    rope(x, case["cos"].to(DEV), case["sin"].to(DEV), out=out)
+    assert torch.equal(out.cpu(), case["out"])
+    rope(x, case["cos"].to(DEV), case["sin"].to(DEV), out=x)
+    assert torch.equal(x.cpu(), case["out"])
+
+
+def test_rope_empty_input():
+    x = torch.empty(1, 0, 2, 128, device=DEV, dtype=torch.bfloat16)
+    t = torch.empty(1, 0, 1, 128, device=DEV)
+    assert rope(x, t, t).shape == x.shape
+
+
+# ---------------------------------------------------------------------------------------
+# Fused RMSNorm + RoPE + ring write
+# ---------------------------------------------------------------------------------------
+def _run_ring(q, k, v, wq, wk, cos, sin, split, grid, offsets, capacity, slots, heads, head_dim, dtype=torch.bfloat16,
+              k_pre=False, heads_per_thread=0):
+    """One fused launch for B streams of one chunk each; returns GPU (q_out, ring_k, ring_v, k_pre)."""
+    B, L, C = q.shape
+    gh, gw = grid
+    hw = gh * gw
+    rows = capacity * hw
+    dq, dk, dv = q.to(DEV), k.to(DEV), v.to(DEV)
+    q_out = torch.empty_like(dq)
+    ring_k = torch.zeros(B * rows, C, device=DEV, dtype=dtype)
+    ring_v = torch.zeros(B * rows, C, device=DEV, dtype=dtype)
+    pre = torch.empty_like(dk) if k_pre else None
+    seqs = [Seq(b * L, L, gh, gw, frame_offset=offsets[b], ring_row=b * rows, ring_frames=capacity, ring_slot0=slots[b])
+            for b in range(B)]
+    qk_norm_rope_kv(heads=heads, head_dim=head_dim, seqs=seqs, cos=cos.to(DEV), sin=sin.to(DEV), q=dq, k=dk, v=dv,
+                    q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v,
+                    k_pre=pre, table_mode="axes", axis_split=split, heads_per_thread=heads_per_thread)
+    torch.cuda.synchronize()
+    return q_out.cpu(), ring_k.view(B, rows, C).cpu(), ring_v.view(B, rows, C).cpu(), (pre.cpu() if k_pre else None)
+
+
+def _check_streams(q, k, v, wq, wk, cos, sin, split, grid, offsets, capacity, slots, heads, head_dim, got):
+    """Compare one launch's outputs with the oracle, stream by stream."""
+    q_out, ring_k, ring_v, k_pre = got
+    B, L, C = q.shape
+    gh, gw = grid
+    hw = gh * gw
+    frames = L // hw
+    ref_k = torch.zeros_like(ring_k)
+    ref_v = torch.zeros_like(ring_v)
+    ref_q = oracle.prep_ring(q, k, v, wq, wk, EPS, cos, sin, split, gh, gw, offsets, ref_k, ref_v, slots)
+    stats = {}
+    stats["q"] = check_bf16_close(q_out, ref_q, "rotated Q")
+    # Ring rows: V bit-exact at the right slots; K within tolerance there; untouched slots still zero.
+    assert torch.equal(ring_v, ref_v), "V ring rows / slot indexing"
+    stats["k"] = check_bf16_close(ring_k, ref_k, "rotated K ring")
+    written = torch.zeros(B, capacity * hw, dtype=torch.bool)
+    for b in range(B):
+        for f in range(frames):
+            slot = (slots[b] + f) % capacity
+            written[b, slot * hw:(slot + 1) * hw] = True
+    assert torch.equal(ring_k[~written], torch.zeros_like(ring_k[~written]))
+    # fp64 yardstick.
+    for b in range(B):
+        ct, st = token_tables(cos, sin, split, offsets[b], frames, gh, gw)
+        exact_q, normed_q = exact_prep(q[b], wq, EPS, ct, st, heads)
+        stats.setdefault("q_rel", []).append(check_against_exact(q_out[b], exact_q, pair_magnitude(normed_q), "Q"))
+    if k_pre is not None:
+        # RoPE and slot placement exactly reproduced from the kernel's own RMSNorm output.
+        stats["k_pre"] = check_bf16_close(k_pre, oracle.rms_norm(k, wk, EPS), "normalised K")
+        recomputed_k = torch.zeros_like(ring_k)
+        scratch_v = torch.zeros_like(ring_v)
+        oracle.prep_ring(k_pre, k_pre, v, wq, wk, EPS, cos, sin, split, gh, gw, offsets, recomputed_k, scratch_v, slots,
+                         norm=False)
+        assert torch.equal(ring_k, recomputed_k), "RoPE of the kernel's normalised K is not bit-exact"
+    return stats
+
+
+@pytest.mark.parametrize("heads_per_thread", [0, 1, 2, 3, 4, 6])
+def test_fused_small_bit_exact_rope_and_slots(heads_per_thread):
+    H, D, gh, gw = 12, 128, 6, 8
+    C = H * D
+    B, frames, capacity = 3, 2, 5
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s) for s in (1, 2, 3))
+    wq, wk = norm_weight(C, 4), norm_weight(C, 5)
+    cos, sin = oracle.rope_tables(D, 64)
+    split = oracle.axis_dims(D)
+    offsets, slots = [3, 17, 40], [4, 0, 2]
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True,
+                    heads_per_thread=heads_per_thread)
+    _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
+
+
+@pytest.mark.parametrize("heads,head_dim", [(2, 8), (2, 16), (1, 128), (3, 64), (40, 128), (24, 128), (5, 32)])
+def test_fused_odd_shapes(heads, head_dim):
+    gh, gw = 3, 4
+    C = heads * head_dim
+    B, frames, capacity = 2, 1, 3
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s) for s in (11, 12, 13))
+    wq, wk = norm_weight(C, 14), norm_weight(C, 15)
+    cos, sin = oracle.rope_tables(head_dim, 32)
+    split = oracle.axis_dims(head_dim)
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), [5, 9], capacity, [1, 2], heads, head_dim, k_pre=True)
+    _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), [5, 9], capacity, [1, 2], heads, head_dim, got)
+
+
+def test_config2_steady_state_ring_of_12():
+    """[1, 1560, 12, 128] chunks at frame offsets 3..20 into a ring of 12
+    frames at slot = offset mod 12; the final ring holds the last 12 chunks at their slots."""
+    H, D, gh, gw, capacity = 12, 128, 30, 52, 12
+    C, hw = H * D, 30 * 52
+    cos, sin = oracle.rope_tables(D, 1024)
+    split = oracle.axis_dims(D)
+    wq, wk = norm_weight(C, 21), norm_weight(C, 22)
+    ring_k = torch.zeros(capacity * hw, C, device=DEV, dtype=torch.bfloat16)
+    ring_v = torch.zeros_like(ring_k)
+    ref_k = torch.zeros(1, capacity * hw, C, dtype=torch.bfloat16)
+    ref_v = torch.zeros_like(ref_k)
+    dcos, dsin, dwq, dwk = cos.to(DEV), sin.to(DEV), wq.to(DEV), wk.to(DEV)
+    for offset in range(3, 21):
+        q, k, v = (randn((1, hw, C), 100 * offset + s) for s in range(3))
+        slot = ops.ring_slot(offset, capacity)
+        assert slot == offset % 12
+        q_out = torch.empty(hw, C, device=DEV, dtype=torch.bfloat16)
+        qk_norm_rope_kv(heads=H, head_dim=D, seqs=[Seq(0, hw, gh, gw, offset, 0, 0, capacity, slot)], cos=dcos,
+                        sin=dsin, q=q[0].to(DEV), k=k[0].to(DEV), v=v[0].to(DEV), q_weight=dwq, k_weight=dwk,
+                        eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v, table_mode="axes")
+        ref_q = oracle.prep_ring(q, k, v, wq, wk, EPS, cos, sin, split, gh, gw, [offset], ref_k, ref_v, [slot])
+        check_bf16_close(q_out.cpu(), ref_q[0], f"Q at offset {offset}")
+    torch.cuda.synchronize()
+    assert torch.equal(ring_v.cpu(), ref_v[0])
+    check_bf16_close(ring_k.cpu(), ref_k[0], "K ring after 18 chunks")
+    # Slot s holds the chunk whose offset is the largest offset <= 20 with offset % 12 == s.
+    for s in range(capacity):
+        offset = max(o for o in range(3, 21) if o % 12 == s)
+        v_expected = randn((1, hw, C), 100 * offset + 2)[0]
+        assert torch.equal(ring_v[s * hw:(s + 1) * hw].cpu(), v_expected), s
+
+
+def test_config3_batched_14b():
+    """8 streams [8, 1560, 40, 128], offsets U{3..40}, per-stream ring of 12."""
+    H, D, gh, gw, capacity = 40, 128, 30, 52, 12
+    C, hw, B = H * D, 30 * 52, 8
+    rng = random.Random(3)
+    offsets = [rng.randint(3, 40) for _ in range(B)]
+    slots = [o % capacity for o in offsets]
+    q, k, v = (randn((B, hw, C), s) for s in (31, 32, 33))
+    wq, wk = norm_weight(C, 34), norm_weight(C, 35)
+    cos, sin = oracle.rope_tables(D, 1024)
+    split = oracle.axis_dims(D)
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True)
+    stats = _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
+    print("config3 parity", stats)
+
+
+def test_config4_varlen_mixed_chunks():
+    """16 streams packed varlen -- 4 first chunks (3x22x40) and 12 steady
+    chunks (1x22x40), H=24, C=3072 -- each into its own ring of 12 frames."""
+    H, D, gh, gw, capacity = 24, 128, 22, 40, 12
+    C, hw = H * D, 22 * 40
+    frames = [3] * 4 + [1] * 12
+    rng = random.Random(4)
+    offsets = [0] * 4 + [rng.randint(3, 40) for _ in range(12)]
+    order = list(range(16))
+    rng.shuffle(order)  # packed in a mixed order
+    cu = [0]
+    for i in order:
+        cu.append(cu[-1] + frames[i] * hw)
+    T = cu[-1]
+    assert T == 4 * 2640 + 12 * 880
+    q, k, v = (randn((T, C), s) for s in (41, 42, 43))
+    wq, wk = norm_weight(C, 44), norm_weight(C, 45)
+    cos, sin = oracle.rope_tables(D, 1024)
+    split = oracle.axis_dims(D)
+    rows = capacity * hw
+    seqs = []
+    for n, i in enumerate(order):
+        seqs.append(Seq(cu[n], frames[i] * hw, gh, gw, frame_offset=offsets[i], ring_row=i * rows,
+                        ring_frames=capacity, ring_slot0=offsets[i] % capacity))
+    dq, dk, dv = q.to(DEV), k.to(DEV), v.to(DEV)
+    q_out = torch.empty_like(dq)
+    ring_k = torch.zeros(16 * rows, C, device=DEV, dtype=torch.bfloat16)
+    ring_v = torch.zeros_like(ring_k)
+    qk_norm_rope_kv(heads=H, head_dim=D, seqs=seqs, cos=cos.to(DEV), sin=sin.to(DEV), q=dq, k=dk, v=dv,
+                    q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v)
+    torch.cuda.synchronize()
+    q_out, ring_k, ring_v = q_out.cpu(), ring_k.view(16, rows, C).cpu(), ring_v.view(16, rows, C).cpu()
+    for n, i in enumerate(order):
+        sl = slice(cu[n], cu[n + 1])
+        ref_k = torch.zeros(1, rows, C, dtype=torch.bfloat16)
+        ref_v = torch.zeros_like(ref_k)
+        ref_q = oracle.prep_ring(q[None, sl], k[None, sl], v[None, sl], wq, wk, EPS, cos, sin, split, gh, gw,
+                                 [offsets[i]], ref_k, ref_v, [offsets[i] % capacity])
+        check_bf16_close(q_out[sl], ref_q[0], f"Q member {i}")
+        check_bf16_close(ring_k[i], ref_k[0], f"K member {i}")
+        assert torch.equal(ring_v[i], ref_v[0]), i
+
+
+def test_config1_fp32_first_chunk():
+    """BASELINE config 1 in fp32: q,k [1, 4680, 12, 128], grid 3x30x52, offset 0 (no ring)."""
+    H, D, gh, gw = 12, 128, 30, 52
+    C, L = H * D, 3 * 30 * 52
+    q, k = (randn((L, C), s, torch.float32) for s in (51, 52))
+    wq, wk = norm_weight(C, 53, torch.float32), norm_weight(C, 54, torch.float32)
+    cos, sin = oracle.rope_tables(D, 1024)
+    split = oracle.axis_dims(D)
+    dq, dk = q.to(DEV), k.to(DEV)
+    q_out, k_out = torch.empty_like(dq), torch.empty_like(dk)
+    qk_norm_rope_kv(heads=H, head_dim=D, seqs=[ops.flat_seq(0, L, gh, gw, 0)], cos=cos.to(DEV), sin=sin.to(DEV),
+                    q=dq, k=dk, q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=k_out)
+    torch.cuda.synchronize()
+    ct, st = token_tables(cos, sin, split, 0, 3, gh, gw)
+    for got, x, w in ((q_out.cpu(), q, wq), (k_out.cpu(), k, wk)):
+        ref = oracle.rope(oracle.rms_norm(x, w, EPS).unflatten(-1, (H, D)), ct[:, None], st[:, None]).flatten(-2)
+        # fp32 end to end: relative error of a few fp32 ulps of the pair magnitude.
+        err = (got.double() - ref.double()).abs()
+        assert bool((err <= 8 * 2.0 ** -24 * pair_magnitude(ref) + 1e-30).all())
+        exact, normed = exact_prep(x, w, EPS, ct, st, H)
+        assert float(((got.double() - exact).abs() / pair_magnitude(normed).clamp_min(1e-30)).max()) < 1e-5
+
+
+def test_empty_sequences_and_zero_tokens():
+    H, D = 2, 128
+    C = H * D
+    cos, sin = oracle.rope_tables(D, 16)
+    x = torch.zeros(8, C, device=DEV, dtype=torch.bfloat16)
+    ring = torch.zeros(8, C, device=DEV, dtype=torch.bfloat16)
+    seqs = [Seq(0, 0, 2, 2, 0, 0, 0, 2, 0), Seq(0, 4, 2, 2, 1, 0, 0, 2, 1), Seq(4, 0, 2, 2, 0, 0, 0, 2, 0)]
+    qk_norm_rope_kv(heads=H, head_dim=D, seqs=seqs, cos=cos.to(DEV), sin=sin.to(DEV), q=x, k=x, v=x,
+                    q_weight=torch.ones(C, device=DEV, dtype=torch.bfloat16),
+                    k_weight=torch.ones(C, device=DEV, dtype=torch.bfloat16), q_out=torch.empty_like(x), k_out=ring,
+                    v_out=ring.clone())
+    torch.cuda.synchronize()
+
+
+def test_qkv_fused_buffer_strides():
+    """Q, K, V as column slices of one [T, 3C] projection output (row stride 3C)."""
+    H, D, gh, gw = 12, 128, 4, 5
+    C, L = H * D, 2 * 4 * 5
+    qkv = randn((L, 3 * C), 61)
+    wq, wk = norm_weight(C, 62), norm_weight(C, 63)
+    cos, sin = oracle.rope_tables(D, 32)
+    split = oracle.axis_dims(D)
+    d = qkv.to(DEV)
+    q_out = torch.empty(L, C, device=DEV, dtype=torch.bfloat16)
+    ring_k = torch.zeros(3 * 20, C, device=DEV, dtype=torch.bfloat16)
+    ring_v = torch.zeros_like(ring_k)
+    qk_norm_rope_kv(heads=H, head_dim=D, seqs=[Seq(0, L, gh, gw, 7, 0, 0, 3, 2)], cos=cos.to(DEV), sin=sin.to(DEV),
+                    q=d[:, :C], k=d[:, C:2 * C], v=d[:, 2 * C:], q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS,
+                    q_out=q_out, k_out=ring_k, v_out=ring_v)
+    torch.cuda.synchronize()
+    q, k, v = qkv[None, :, :C], qkv[None, :, C:2 * C], qkv[None, :, 2 * C:]
+    ref_k = torch.zeros(1, 60, C, dtype=torch.bfloat16)
+    ref_v = torch.zeros_like(ref_k)
+    ref_q = oracle.prep_ring(q, k, v, wq, wk, EPS, cos, sin, split, gh, gw, [7], ref_k, ref_v, [2])
+    check_bf16_close(q_out.cpu(), ref_q[0], "Q from QKV buffer")
+    check_bf16_close(ring_k.cpu(), ref_k[0], "K from QKV buffer")
+    assert torch.equal(ring_v.cpu(), ref_v[0])
+
+
+# ---------------------------------------------------------------------------------------
+# The drop-in processor and the ring layout against the reference's recorded prep
+# ---------------------------------------------------------------------------------------
+class _Replay(torch.nn.Module):
+    """Stands in for a projection: returns the recorded projection output."""
+
+    def __init__(self):
+        super().__init__()
+        self.value = None
+
+    def forward(self, hidden):
+        return self.value
+
+
+def _attn(g):
+    heads, C = g["heads"], g["heads"] * g["head_dim"]
+    attn = torch.nn.Module()
+    attn.heads = heads
+    attn.to_q, attn.to_k, attn.to_v = _Replay(), _Replay(), _Replay()
+    attn.norm_q, attn.norm_k = torch.nn.RMSNorm(C, eps=g["eps"]), torch.nn.RMSNorm(C, eps=g["eps"])
+    out = torch.nn.Linear(C, C)
+    state = g["attn_state"]
+    out.weight.data, out.bias.data = state["to_out.0.weight"].float(), state["to_out.0.bias"].float()
+    attn.to_out = torch.nn.ModuleList([out, torch.nn.Dropout(0.0)])
+    attn.norm_q.weight.data = g["norm_q_weight"].float()
+    attn.norm_k.weight.data = g["norm_k_weight"].float()
+    return attn.to(DEV, torch.bfloat16)
+
+
+def test_drop_in_processor_matches_reference_prep(golden):
+    """physisserve_b200.wan.Attention over the recorded 24-chunk request: Q', K window', V
+    window and the output of the block's attention, with the engine's Cache contract."""
+    g = golden("attention.pt")
+    heads, D = g["heads"], g["head_dim"]
+    attn = _attn(g)
+    processor = Attention()
+    records = {r["chunk"]: r for r in g["records"]}
+    pages = {}
+    captured = {}
+    import physisserve_b200.wan as wan_mod
+    original = wan_mod.F.scaled_dot_product_attention
+
+    def spy(q, k, v, *a, **kw):
+        captured["sdpa"] = (q, k, v)
+        return original(q, k, v, *a, **kw)
+
+    wan_mod.F.scaled_dot_product_attention = spy
+    try:
+        for chunk, inputs in enumerate(g["inputs"]):
+            history = oracle.history_chunks(chunk)
+            cache = oracle.Cache([pages[p] for p in history])
+            processor.cache = cache
+            for name in ("q", "k", "v"):
+                getattr(attn, f"to_{name}").value = inputs[name].to(DEV)
+            rec = records.get(chunk)
+            if rec is not None:
+                own = tuple(t.to(DEV) for t in rec["own"])
+                window = tuple(t.to(DEV) for t in rec["window"])
+            else:
+                own = window = None
+            if rec is None:
+                # Reuse the previous recorded tables' geometry: rebuild with the oracle.
+                gh, gw = g["grid"]
+                geometry = oracle.Chunks((1, 16, 1, 2 * gh, 2 * gw), g["count"], oracle.WAN_FIRST_FRAMES)
+                split = oracle.axis_dims(D)
+                parts = [oracle.frames_table(g["freqs_cos"], g["freqs_sin"], split, f, f + geometry.frames_of(p), gh, gw)
+                         for p, f in oracle.window_positions(geometry, chunk)]
+                window = tuple(torch.cat([p[i] for p in parts], dim=1).to(DEV) for i in (0, 1))
+                own = tuple(t.to(DEV) for t in parts[-1])
+            with torch.inference_mode():
+                out = processor(attn, torch.empty(1, device=DEV), rotary_emb=(own, window))
+            pages[chunk] = cache.page
+            if rec is None:
+                continue
+            q_rot, k_rot, v_win = (t.cpu() for t in captured["sdpa"])
+            check_bf16_close(q_rot, rec["q_rot"], f"Q' chunk {chunk}")
+            check_bf16_close(k_rot, rec["k_window_rot"], f"K window' chunk {chunk}")
+            assert torch.equal(v_win, rec["v_window"]), chunk
+            check_bf16_close(cache.page[0].contiguous().cpu(), rec["page_k"], f"page K chunk {chunk}")
+            torch.testing.assert_close(out.float().cpu(), rec["out"].float(), atol=3e-2, rtol=3e-2)
+    finally:
+        wan_mod.F.scaled_dot_product_attention = original
+
+
+def test_ring_layout_matches_reference_window(golden):
+    """prep_ring over the recorded request: the ring's window rows (sink re-rotated at its
+    relocated position, recent chunks at their slots) equal the reference's rotated window."""
+    g = golden("attention.pt")
+    heads, D = g["heads"], g["head_dim"]
+    gh, gw = g["grid"]
+    C = heads * D
+    hw = gh * gw
+    cos, sin = g["freqs_cos"].to(DEV), g["freqs_sin"].to(DEV)
+    wq, wk = g["norm_q_weight"].to(DEV), g["norm_k_weight"].to(DEV)
+    cache = RingCache(heads=heads, head_dim=D, grid_h=gh, grid_w=gw, device=DEV)
+    records = {r["chunk"]: r for r in g["records"]}
+    for chunk, inputs in enumerate(g["inputs"]):
+        pos = window_layout(chunk)
+        q_rot = prep_ring(inputs["q"].to(DEV), inputs["k"].to(DEV), inputs["v"].to(DEV), wq, wk, g["eps"], cos, sin,
+                          cache, [pos])
+        rec = records.get(chunk)
+        if rec is None:
+            continue
+        check_bf16_close(q_rot.view(1, -1, heads, D).transpose(1, 2).cpu(), rec["q_rot"], f"Q' chunk {chunk}")
+        kw, vw = cache.window(chunk)
+        want_k = rec["k_window_rot"][0].transpose(0, 1).flatten(1)   # [tokens, C] reference order
+        want_v = rec["v_window"][0].transpose(0, 1).flatten(1)
+        got_k = kw[0].transpose(0, 1).flatten(1).cpu()
+        got_v = vw[0].transpose(0, 1).flatten(1).cpu()
+        # Map our rows (sink | ring slots) to the reference window order.
+        order = list(range(cache.sink_rows))
+        pages = [p for p in oracle.history_chunks(chunk) if p != 0] + ([chunk] if chunk else [])
+        for page in pages:
+            slot = cache.slot(page)
+            base = cache.sink_rows + slot * hw
+            order.extend(range(base, base + hw))
+        got_k, got_v = got_k[order], got_v[order]
+        check_bf16_close(got_k, want_k, f"ring window K chunk {chunk}")
+        assert torch.equal(got_v, want_v), chunk
+
+
+def test_prepare_reference_layout_batch_members(golden):
+    """Same-block batch (block_batch): per-member own tables in one launch."""
+    g = golden("attention.pt")
+    b = g["batch"]
+    heads, D = g["heads"], g["head_dim"]
+    q_rot, k_pre = prepare_reference_layout(b["q"].to(DEV), b["k"].to(DEV), heads, g["norm_q_weight"].to(DEV),
+                                            g["norm_k_weight"].to(DEV), g["eps"],
+                                            tuple(t.to(DEV) for t in b["own"]))
+    check_bf16_close(q_rot.view(2, -1, heads, D).transpose(1, 2).cpu(), b["q_rot"], "batch Q'")
+    for m in range(2):
+        check_bf16_close(k_pre[m:m + 1].view(1, -1, heads, D).transpose(1, 2).contiguous().cpu(), b["pages_k"][m],
+                         f"batch page {m}")
