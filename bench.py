@@ -61,10 +61,13 @@ WORKLOADS = {
 class Workload:
     """Device buffers and launch list of one rank's share of a workload."""
 
-    def __init__(self, name, rank, world, device, seed=1234):
+    def __init__(self, name, rank, world, device, seed=1234, ring_frames=None, heads_per_thread=0, **tiling):
         from physisserve_b200.wan import wan_rope_tables
 
-        spec = WORKLOADS[name]
+        spec = dict(WORKLOADS[name])
+        if ring_frames:
+            spec["capacity"] = ring_frames
+        self.tiling = dict(heads_per_thread=heads_per_thread, **tiling)
         self.name, self.spec, self.device = name, spec, device
         self.heads, self.head_dim = spec["heads"], spec["head_dim"]
         self.C = self.heads * self.head_dim
@@ -138,7 +141,7 @@ class Workload:
                                 seqs=[Seq(0, self.hw, self.gh, self.gw, offset, 0, 0, self.capacity,
                                           offset % self.capacity)],
                                 cos=self.cos, sin=self.sin, q=q, k=k, v=v, q_weight=self.wq[0], k_weight=self.wk[0],
-                                eps=1e-6, q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v)
+                                eps=1e-6, q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v, **self.tiling)
             return 18
         seqs = self.seqs(step)
         n = 0
@@ -147,7 +150,7 @@ class Workload:
             block = cell % self.n_blocks
             qk_norm_rope_kv(heads=self.heads, head_dim=self.head_dim, seqs=seqs, cos=self.cos, sin=self.sin, q=q, k=k,
                             v=v, q_weight=self.wq[block], k_weight=self.wk[block], eps=1e-6, q_out=self.q_out,
-                            k_out=self.ring_k, v_out=self.ring_v)
+                            k_out=self.ring_k, v_out=self.ring_v, **self.tiling)
             n += 1
         return n
 
@@ -379,7 +382,13 @@ def run_ours(args):
     from physisserve_b200 import _lib
 
     _lib.load()
-    work = Workload(args.workload, rank, world, device)
+    work = Workload(args.workload, rank, world, device, ring_frames=args.ring_frames,
+                    heads_per_thread=args.heads_per_thread, kernel=args.kernel, stages=args.stages,
+                    groups=args.groups, ctas_per_sm=args.ctas_per_sm, row_threads=args.row_threads,
+                    release=args.release, vstages=args.vstages)
+    if args.cells:
+        work.launches_per_step = args.cells
+        work.tokens_per_step = work.tokens_per_launch * args.cells
     stream = torch.cuda.current_stream(device)
 
     graph = None
@@ -432,7 +441,7 @@ def run_ours(args):
     peak, peak_src = measured_peak()
 
     # End to end through the public API: pinned host inputs -> device -> prep -> q' to host.
-    e2e = run_e2e(args, work, world, device, stream)
+    e2e = None if args.no_e2e else run_e2e(args, work, world, device, stream)
 
     all_clocks = gather_objects(clocks, world)
     cpu = None
@@ -444,6 +453,7 @@ def run_ours(args):
 
     if rank == 0:
         spec = WORKLOADS[args.workload]
+        config_extra = {"ring_frames_override": args.ring_frames} if args.ring_frames else {}
         line = {
             "metric": "rotated_qk_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -491,7 +501,7 @@ def run_e2e(args, work, world, device, stream):
             d.copy_(h, non_blocking=True)
         qk_norm_rope_kv(heads=work.heads, head_dim=work.head_dim, seqs=work.seqs(i), cos=work.cos, sin=work.sin,
                         q=dev_in[0], k=dev_in[1], v=dev_in[2], q_weight=work.wq[0], k_weight=work.wk[0], eps=1e-6,
-                        q_out=work.q_out, k_out=work.ring_k, v_out=work.ring_v)
+                        q_out=work.q_out, k_out=work.ring_k, v_out=work.ring_v, **work.tiling)
         host_out.copy_(work.q_out, non_blocking=True)
 
     for i in range(3):
@@ -521,6 +531,18 @@ def main(argv=None):
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--e2e-steps", type=int, default=20)
+    parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    parser.add_argument("--ring-frames", type=int, default=None,
+                        help="ring capacity override (smaller device footprint for profiling runs)")
+    parser.add_argument("--heads-per-thread", type=int, default=0, help="kernel tiling override (0 = automatic)")
+    parser.add_argument("--kernel", choices=("auto", "bulk", "rows"), default="auto")
+    parser.add_argument("--stages", type=int, default=0, help="bulk kernel: smem stages per CTA (0 = fit)")
+    parser.add_argument("--groups", type=int, default=0, help="bulk kernel: consumer row groups (0 = auto)")
+    parser.add_argument("--ctas-per-sm", type=int, default=0, help="bulk kernel: persistent CTAs per SM")
+    parser.add_argument("--row-threads", type=int, default=0, help="bulk kernel: threads per row group")
+    parser.add_argument("--release", type=int, default=0, help="bulk kernel: stage release mode (0 auto, 1, 2)")
+    parser.add_argument("--vstages", type=int, default=0, help="bulk kernel: V stages per CTA (0 = auto)")
+    parser.add_argument("--cells", type=int, default=0, help="launches per step override (profiling runs)")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")

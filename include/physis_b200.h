@@ -79,6 +79,12 @@ typedef enum ps_table_mode {
   PS_TABLE_AXES = 1
 } ps_table_mode;
 
+typedef enum ps_kernel {
+  PS_KERNEL_AUTO = 0,  /* bulk-copy pipeline when a 3-row stage fits shared memory, else rows */
+  PS_KERNEL_ROWS = 1,  /* one row group per token, 128-bit register loads */
+  PS_KERNEL_BULK = 2   /* persistent CTAs streaming rows through shared memory with cp.async.bulk */
+} ps_kernel;
+
 /* One sequence of a ps_qk_norm_rope_kv call: a stream's chunk, a batch member
  * of WanDiT.block_batch (wan.py:291-314) or a varlen member. */
 typedef struct ps_seq {
@@ -106,7 +112,17 @@ typedef struct ps_qk_prep_args {
   int32_t t_dim, h_dim, w_dim; /* axis split of D (even parts summing to D); PS_TABLE_AXES only */
   int32_t n_seqs;       /* 1..PS_MAX_SEQS */
   float eps;            /* RMSNorm epsilon */
-  int32_t heads_per_thread; /* tiling: heads each thread covers (divides H); 0 = automatic */
+  int32_t heads_per_thread; /* PS_KERNEL_ROWS: heads each thread covers (divides H); 0 = automatic */
+  int32_t kernel;       /* ps_kernel */
+  int32_t stages;       /* PS_KERNEL_BULK: shared-memory row stages per CTA; 0 = as many as fit */
+  int32_t groups;       /* PS_KERNEL_BULK: consumer row groups per CTA; 0 = automatic */
+  int32_t ctas_per_sm;  /* PS_KERNEL_BULK: persistent CTAs per SM; 0 = 1 */
+  int32_t row_threads;  /* PS_KERNEL_BULK: threads per row group (multiple of 32); 0 = automatic */
+  int32_t release;      /* PS_KERNEL_BULK: 0 = automatic, 1 = free a stage as soon as its stores have
+                           read it, 2 = keep one store group in flight per row group (free the
+                           previous stage after the next token's stores are issued) */
+  int32_t vstages;      /* PS_KERNEL_BULK: shared-memory V stages per CTA; 0 = automatic */
+  int32_t reserved1;    /* must be 0 */
 
   int64_t in_rows;      /* rows of q, k, v, q_out, k_pre (bounds of token_start + n_tokens) */
   const void* q;  int64_t q_stride;   /* [in_rows, C]; NULL: no Q role */
@@ -153,6 +169,12 @@ PS_API int32_t ps_qk_prep_validate(const ps_qk_prep_args* args);
  * rn(rn(e*s)+rn(o*c)) in fp32 from the rounded RMSNorm output and rounds once
  * to the element type (_rope, wan.py:58-63). */
 PS_API int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream);
+
+
+/* Number of bounded waits inside ps_qk_norm_rope_kv's bulk kernel that ran out
+ * (a wait gives up after ~2 s, the CTA then drains its copies and returns) on the
+ * current device since the last reset.  Synchronises the device first. */
+PS_API int32_t ps_device_timeouts(uint32_t* count, int32_t reset);
 
 /* Drop-in for _rope(x, cosine, sine) (wan.py:58-63) on a strided 4-D tensor.
  *   x, out:   [B, L, H, D] with element strides x_strides[0..2], out_strides[0..2]

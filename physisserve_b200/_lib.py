@@ -25,9 +25,11 @@ STATUS_NAMES = {
 BF16, F32 = 0, 1
 # ps_table_mode
 TABLE_TOKENS, TABLE_AXES = 0, 1
+# ps_kernel
+KERNEL_AUTO, KERNEL_ROWS, KERNEL_BULK = 0, 1, 2
 
 EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
-           "ps_rope", "ps_rope_validate")
+           "ps_device_timeouts", "ps_rope", "ps_rope_validate")
 
 
 class PsSeq(ctypes.Structure):
@@ -60,6 +62,14 @@ class PsQkPrepArgs(ctypes.Structure):
         ("n_seqs", ctypes.c_int32),
         ("eps", ctypes.c_float),
         ("heads_per_thread", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("groups", ctypes.c_int32),
+        ("ctas_per_sm", ctypes.c_int32),
+        ("row_threads", ctypes.c_int32),
+        ("release", ctypes.c_int32),
+        ("vstages", ctypes.c_int32),
+        ("reserved1", ctypes.c_int32),
         ("in_rows", ctypes.c_int64),
         ("q", ctypes.c_void_p), ("q_stride", ctypes.c_int64),
         ("k", ctypes.c_void_p), ("k_stride", ctypes.c_int64),
@@ -105,6 +115,8 @@ def load() -> ctypes.CDLL:
     lib.ps_qk_prep_validate.argtypes = [ctypes.POINTER(PsQkPrepArgs)]
     lib.ps_qk_norm_rope_kv.restype = ctypes.c_int32
     lib.ps_qk_norm_rope_kv.argtypes = [ctypes.POINTER(PsQkPrepArgs), ctypes.c_void_p]
+    lib.ps_device_timeouts.restype = ctypes.c_int32
+    lib.ps_device_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
     i64p = ctypes.POINTER(ctypes.c_int64)
     rope_args = [ctypes.c_int32, ctypes.c_void_p, i64p, ctypes.c_void_p, ctypes.c_void_p, i64p, ctypes.c_void_p,
                  i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]

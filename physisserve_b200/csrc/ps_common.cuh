@@ -42,9 +42,14 @@ template <> struct Vec16<__nv_bfloat16> {
     }
     return make_uint4(w[0], w[1], w[2], w[3]);
   }
-  // Rounds an fp32 value to the element type and back (exact widening).
-  __device__ __forceinline__ static float round(float x) {
-    return __bfloat162float(__float2bfloat16_rn(x));
+  // Rounds two fp32 values to the element type and back (exact widening).  The
+  // paired conversion (cvt.rn.bf16x2.f32) keeps the rounding off the XU pipe that a
+  // per-element float->bf16 conversion would saturate.
+  __device__ __forceinline__ static void round_pair(float& a, float& b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
+    a = __uint_as_float(u << 16);
+    b = __uint_as_float(u & 0xffff0000u);
   }
 };
 
@@ -60,14 +65,16 @@ template <> struct Vec16<float> {
     return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
                       __float_as_uint(f[3]));
   }
-  __device__ __forceinline__ static float round(float x) { return x; }
+  __device__ __forceinline__ static void round_pair(float&, float&) {}
 };
 
 // Read-once activation loads: read-only path without L1 allocation, so the
-// streamed rows do not displace the RoPE tables / weights held in L1.
+// streamed rows do not displace the RoPE tables / weights held in L1.  Volatile
+// keeps every load of a row where it is written -- ahead of the first use -- so a
+// thread has all of its row's 16-byte vectors in flight at once.
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
   uint4 r;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
@@ -78,9 +85,85 @@ __device__ __forceinline__ uint4 ld_keep(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
+// Division by a per-sequence constant d >= 1 with a host-computed magic number
+// m = floor((2^64 - 1) / d) + 1 (m = 0 encodes d == 1): floor(n / d) =
+// umulhi64(n, m) exactly for all n, d < 2^32, since n*m / 2^64 exceeds n / d by
+// less than n / 2^64 < 1 / d.
+__host__ __device__ inline uint64_t div_magic(uint32_t d) {
+  return d <= 1 ? 0 : (~0ull) / d + 1;
+}
+__device__ __forceinline__ uint32_t div_by(uint32_t n, uint64_t magic) {
+  return magic == 0 ? n : static_cast<uint32_t>(__umul64hi(static_cast<uint64_t>(n), magic));
+}
+
 __device__ __forceinline__ void st_vec(void* p, const uint4& v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
+
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100's paired FP32 instructions).  Each lane of
+// a pair is rounded exactly as the scalar IEEE operation would round it.
+// ---------------------------------------------------------------------------
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 f2_make(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(f32x2 v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// A 16-byte vector as P = E/2 element pairs (even, odd) in fp32x2 registers,
+// and back with one rounding to the element type.
+template <typename T> struct Pairs16;
+
+template <> struct Pairs16<__nv_bfloat16> {
+  static constexpr int kPairs = 4;
+  __device__ __forceinline__ static void unpack(const uint4& u, f32x2* x) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = f2_make(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+  }
+  __device__ __forceinline__ static uint32_t pack_pair(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* lo, const float* hi) {
+    return make_uint4(pack_pair(lo[0], hi[0]), pack_pair(lo[1], hi[1]), pack_pair(lo[2], hi[2]),
+                      pack_pair(lo[3], hi[3]));
+  }
+  // Rounds each lane of a pair to bf16 and widens it back (exactly).
+  __device__ __forceinline__ static f32x2 round(f32x2 v) {
+    float a, b;
+    f2_split(v, a, b);
+    const uint32_t u = pack_pair(a, b);
+    return f2_make(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+  }
+};
+
+template <> struct Pairs16<float> {
+  static constexpr int kPairs = 2;
+  __device__ __forceinline__ static void unpack(const uint4& u, f32x2* x) {
+    x[0] = f2_make(__uint_as_float(u.x), __uint_as_float(u.y));
+    x[1] = f2_make(__uint_as_float(u.z), __uint_as_float(u.w));
+  }
+  __device__ __forceinline__ static uint4 pack(const float* lo, const float* hi) {
+    return make_uint4(__float_as_uint(lo[0]), __float_as_uint(hi[0]), __float_as_uint(lo[1]), __float_as_uint(hi[1]));
+  }
+  __device__ __forceinline__ static f32x2 round(f32x2 v) { return v; }
+};
 
 // The even/odd rotation of one element pair exactly as _rope evaluates it
 // (wan.py:61-62): each product and the difference/sum rounded separately in

@@ -1,21 +1,36 @@
 // Fused Q/K RMSNorm + 3D RoPE + K/V history-ring write for sm_100a.
 //
 // One launch covers every token of up to PS_MAX_SEQS sequences (streams, batch
-// members of WanDiT.block_batch, or varlen members).  A "row group" of tpr
-// threads owns one token row of C = H*D elements at a time:
-//   * thread lt of the group owns the 16-byte vector dvec = lt % vph of every
-//     head it covers (vph = vectors per head), heads head0 + i*hstep for
-//     i < V, so its head-dim slice -- and therefore its cos/sin values -- is
-//     the same for all of its V heads and is loaded once per token;
-//   * sum(x^2) over the whole row (the reference's RMSNorm spans all heads,
-//     wan.py:104-105) is reduced with xor shuffles inside power-of-two lane
-//     segments, then across segments through shared memory in a fixed order,
-//     so every thread of the group obtains bit-identical sums;
-//   * V copies, Q/K loads and stores are 128-bit, coalesced along the row.
-// The path is purely elementwise + row reduction, so it is bound by HBM
-// bandwidth: 12*C bytes per token (read q,k,v; write q', k'-slot, v-slot) for
-// bf16.  No tensor cores, no TMA: the row-group loads are already full-line
-// coalesced, and the per-axis cos/sin rows (<= a few KB per CTA) stay in L1.
+// members of WanDiT.block_batch, or varlen members).  The work per token row
+// (C = H*D elements of each of q, k, v) is:
+//   * sum(x^2) over the whole row of q and of k (the reference's RMSNorm spans
+//     all heads, wan.py:104-105), y = (x * rstd) * w rounded to the element type;
+//   * RoPE of each element pair of y with the token's cos/sin (wan.py:58-63);
+//   * rotated q to q_out, rotated k and the untouched v to the ring slot of the
+//     token's frame.
+// It is HBM-bound: 12*C bytes per token (read q,k,v; write q', k'-slot, v-slot)
+// for bf16.  Two kernels implement it:
+//
+// bulk_kernel (default) -- a persistent CTA per SM.  One producer thread streams
+//   whole q/k/v rows into a ring of shared-memory stages with cp.async.bulk
+//   (the TMA bulk-copy engine) completing on per-stage mbarriers; consumer row
+//   groups normalise and rotate q and k in place in shared memory, and the rows
+//   leave with cp.async.bulk stores (v goes global -> smem -> ring without
+//   touching registers).  Loads of the next stages are in flight while a stage
+//   is computed, so latency is hidden without holding rows in registers.
+// rows_kernel -- one row group per token with 128-bit register loads; used for
+//   rows too wide for a shared-memory stage and as the reference tiling.
+//
+// Inside a row group of tpr threads, thread lt owns the 16-byte vector
+// dvec = lt % vph of each of its V heads (head0 + i*hstep, vph = vectors per
+// head), so its head-dim slice -- and its cos/sin values -- is the same for all
+// of its heads.  Row sums are reduced with xor shuffles inside power-of-two lane
+// segments, then across segments through shared memory in a fixed order, so
+// every thread of the group obtains bit-identical sums.
+//
+// Every wait on an mbarrier is bounded by a deadline of ~2 s of %globaltimer;
+// a wait that runs out bumps a device counter (ps_device_timeouts) and the CTA
+// drains its own copies and returns instead of spinning.
 
 #include <stdio.h>
 #include <string.h>
@@ -23,12 +38,18 @@
 #include "ps_common.cuh"
 
 namespace ps {
+
+// Count of bounded waits that ran out, per device (read by ps_device_timeouts).
+__device__ unsigned int g_wait_timeouts;
+
 namespace {
 
 struct DevSeq {
   int64_t row0;       // token_start
   int64_t table_row;  // PS_TABLE_TOKENS row of token 0
   int64_t ring_row;   // ring slot 0 row in k_out / v_out
+  uint64_t hw_magic;  // div_magic(hw)
+  uint64_t gw_magic;  // div_magic(gw)
   int32_t hw;         // grid_h * grid_w
   int32_t gw;
   int32_t frame_offset;
@@ -76,53 +97,177 @@ struct KParams {
   int32_t total;  // tokens over all sequences
   float eps;
   float c_f;      // (float)C
+  // bulk_kernel only
+  int32_t stages;       // shared-memory stages per CTA
+  int32_t row_bytes;    // C * element size
+  int32_t stage_bytes;  // bytes of one stage (q | k | v rows)
+  int32_t load_bytes;   // bytes the producer loads into a stage
+  int32_t defer;        // 1: free a stage only after the group's next stores are issued
+  int32_t vstages;      // shared-memory V stages per CTA
+  int32_t vstage_bytes;
+  int32_t off_abort, off_partials, off_meta, off_vmeta, off_stages, off_vstages;
   int32_t cum[PS_MAX_SEQS + 1];
   DevSeq seq[PS_MAX_SEQS];
 };
-static_assert(sizeof(KParams) <= 4096, "kernel parameters must fit the classic 4 KB space");
+// Up to 32764 bytes of kernel parameters are accepted by the CUDA 12.1+ driver on
+// Volta and newer; this stays well inside that limit.
+static_assert(sizeof(KParams) <= 8192, "kernel parameters too large");
 
-// CTA size cap: 512 threads leave 128 registers per thread, enough for the
-// V <= 8 vectors of Q and K a thread holds while the row sum is reduced.
+// CTA size cap of rows_kernel: 512 threads leave 128 registers per thread, enough
+// for the V <= 8 vectors of Q and K a thread holds while the row sum is reduced.
 constexpr int kMaxThreads = 512;
+// bulk_kernel: consumer threads per CTA at most (plus one producer warp).
+constexpr int kBulkMaxConsumers = 384;
+constexpr int kBulkMaxGroups = 15;           // named barriers 1..15
+constexpr int kBulkSmemBudget = 227 * 1024;  // dynamic shared memory per CTA (sm_100 maximum)
+constexpr unsigned long long kWaitNs = 2000000000ull;
 
+// ------------------------------------------------------------------------------------
+// Token decode and per-thread RoPE coefficients (shared by both kernels)
+// ------------------------------------------------------------------------------------
+struct Token {
+  int64_t row;     // row in q/k/v/q_out/k_pre
+  int64_t kv_row;  // ring row of k_out/v_out
+  int64_t trow_t, trow_h, trow_w;  // table rows of the frame / row / column segments
+};
+
+__device__ __forceinline__ int find_seq(const KParams& p, int g) {
+  int lo = 0, hi = p.n_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.cum[mid] <= g) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ Token decode(const KParams& p, int g) {
+  const int s = find_seq(p, g);
+  const DevSeq& sq = p.seq[s];
+  const int l = g - p.cum[s];
+  const int f = static_cast<int>(div_by(static_cast<uint32_t>(l), sq.hw_magic));
+  const int rr = l - f * sq.hw;
+  Token t;
+  t.row = sq.row0 + l;
+  int slot = sq.ring_slot0 + f;  // slot0 < ring_frames and f < frames <= ring_frames
+  if (slot >= sq.ring_frames) slot -= sq.ring_frames;
+  t.kv_row = sq.ring_row + static_cast<int64_t>(slot) * sq.hw + rr;
+  if (p.table_mode == PS_TABLE_AXES) {
+    const int hh = static_cast<int>(div_by(static_cast<uint32_t>(rr), sq.gw_magic));
+    t.trow_t = sq.frame_offset + f;
+    t.trow_h = hh;
+    t.trow_w = rr - hh * sq.gw;
+  } else {
+    t.trow_t = t.trow_h = t.trow_w = sq.table_row + l;
+  }
+  return t;
+}
+
+template <int P>
+struct Rot {
+  float ce[P], co[P], se[P], so[P];
+};
+
+template <int P>
+__device__ __forceinline__ void load_rot(const KParams& p, const Token& t, int dvec, Rot<P>& r) {
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int pair = dvec * P + j;
+    const int64_t trow = pair < p.tp ? t.trow_t : (pair < p.thp ? t.trow_h : t.trow_w);
+    const float2 c = __ldg(reinterpret_cast<const float2*>(p.cos + trow * p.head_dim + 2 * pair));
+    const float2 s = __ldg(reinterpret_cast<const float2*>(p.sin + trow * p.head_dim + 2 * pair));
+    r.ce[j] = c.x;
+    r.co[j] = c.y;
+    r.se[j] = s.x;
+    r.so[j] = s.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float sum_squares(const uint4& v) {
+  constexpr int E = Vec16<T>::kElems;
+  float x[E];
+  Vec16<T>::unpack(v, x);
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc = fmaf(x[e], x[e], acc);
+  return acc;
+}
+
+// y = round((x * rstd) * w) -- torch.nn.RMSNorm's single rounding to the element type.
+template <typename T>
+__device__ __forceinline__ void normalise(float* x, const uint4& wv, float rstd) {
+  constexpr int E = Vec16<T>::kElems;
+  float w[E];
+  Vec16<T>::unpack(wv, w);
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], rstd), w[e]);
+#pragma unroll
+  for (int e = 0; e < E; e += 2) Vec16<T>::round_pair(x[e], x[e + 1]);
+}
+
+template <typename T, int P>
+__device__ __forceinline__ uint4 rotate(const float* x, const Rot<P>& r) {
+  float y[2 * P];
+#pragma unroll
+  for (int j = 0; j < P; ++j)
+    rotate_pair(x[2 * j], x[2 * j + 1], r.ce[j], r.co[j], r.se[j], r.so[j], y[2 * j], y[2 * j + 1]);
+  return Vec16<T>::pack(y);
+}
+
+__device__ __forceinline__ float rstd_of(float ssq, float c, float eps) {
+  // 1 / sqrt(mean(x^2) + eps), each step IEEE-rounded (torch's CPU rsqrt is 1/sqrt).
+  return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssq, c), eps)));
+}
+
+// Reduces (sum q^2, sum k^2) over the tpr threads of a row group; every thread of the
+// group receives bit-identical sums.  `sync` orders the shared partials.
+template <typename Sync>
+__device__ __forceinline__ void reduce_row(const KParams& p, float2* partials, int lt, float& sq, float& sk,
+                                           Sync sync) {
+  for (int o = p.seg >> 1; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    sk += __shfl_xor_sync(0xffffffffu, sk, o);
+  }
+  if (p.nseg > 1) {
+    if ((lt % p.seg) == 0) partials[lt / p.seg] = make_float2(sq, sk);
+    sync();
+    float a = 0.f, b = 0.f;
+    for (int i = 0; i < p.nseg; ++i) {
+      const float2 t = partials[i];
+      a += t.x;
+      b += t.y;
+    }
+    sq = a;
+    sk = b;
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// rows_kernel: one row group per token, register loads
+// ------------------------------------------------------------------------------------
 template <typename T, int V>
-__global__ void __launch_bounds__(kMaxThreads) qk_prep_kernel(const __grid_constant__ KParams p) {
+__global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant__ KParams p) {
   using VT = Vec16<T>;
-  constexpr int E = VT::kElems;  // elements per 16-byte vector
-  constexpr int P = E / 2;       // rotation pairs per vector
-  extern __shared__ float2 partials[];  // [rows][nseg] (sum q^2, sum k^2)
+  constexpr int E = VT::kElems;
+  constexpr int P = E / 2;
+  extern __shared__ float2 partials[];  // [rows][nseg]
 
   const int rg = threadIdx.x / p.tpr;
   const int lt = threadIdx.x - rg * p.tpr;
   const int dvec = lt % p.vph;
   const int head0 = lt / p.vph;
-  const int64_t g = static_cast<int64_t>(blockIdx.x) * p.rows + rg;
+  const int g = blockIdx.x * p.rows + rg;
   const bool active = g < p.total;
   const int flags = p.flags;
-
-  // Sequence of token g: last s with cum[s] <= g (uniform per row group).
-  int s = 0;
-  if (active) {
-    int lo = 0, hi = p.n_seqs - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (p.cum[mid] <= g) lo = mid; else hi = mid - 1;
-    }
-    s = lo;
-  }
-  const DevSeq& sq = p.seq[s];
-  const int l = active ? static_cast<int>(g - p.cum[s]) : 0;
-  const int64_t row = sq.row0 + l;
-  const int f = l / sq.hw;
-  const int rr = l - f * sq.hw;
+  const Token t = decode(p, active ? g : 0);
 
   int elem_off[V];
 #pragma unroll
   for (int i = 0; i < V; ++i) elem_off[i] = (head0 + i * p.hstep) * p.head_dim + dvec * E;
 
-  const T* qrow = static_cast<const T*>(p.q) + row * p.q_stride;
-  const T* krow = static_cast<const T*>(p.k) + row * p.k_stride;
-  const T* vrow = static_cast<const T*>(p.v) + row * p.v_stride;
+  const T* qrow = static_cast<const T*>(p.q) + t.row * p.q_stride;
+  const T* krow = static_cast<const T*>(p.k) + t.row * p.k_stride;
+  const T* vrow = static_cast<const T*>(p.v) + t.row * p.v_stride;
 
   uint4 qv[V], kv[V];
   if (active) {
@@ -132,137 +277,431 @@ __global__ void __launch_bounds__(kMaxThreads) qk_prep_kernel(const __grid_const
       if (flags & kHasK) kv[i] = ld_stream(krow + elem_off[i]);
     }
   }
-
-  // Destination row of K / V: ring slot of the token's frame.
-  int64_t kv_row = 0;
-  if (active && (flags & (kKOut | kHasV))) {
-    int slot = sq.ring_slot0 + f;
-    slot = slot % sq.ring_frames;
-    kv_row = sq.ring_row + static_cast<int64_t>(slot) * sq.hw + rr;
-  }
-
   if (active && (flags & kHasV)) {
     uint4 vv[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) vv[i] = ld_stream(vrow + elem_off[i]);
-    T* vout = static_cast<T*>(p.v_out) + kv_row * p.v_out_stride;
+    T* vout = static_cast<T*>(p.v_out) + t.kv_row * p.v_out_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) st_vec(vout + elem_off[i], vv[i]);
   }
+  Rot<P> r;
+  if (active && (flags & (kHasQ | kHasK))) load_rot<P>(p, t, dvec, r);
 
-  // cos / sin of this thread's P pairs.
-  float ce[P], co[P], se[P], so[P];
-  if (active && (flags & (kHasQ | kHasK))) {
-    int64_t trow_t, trow_h, trow_w;
-    if (p.table_mode == PS_TABLE_AXES) {
-      const int hh = rr / sq.gw;
-      trow_t = sq.frame_offset + f;
-      trow_h = hh;
-      trow_w = rr - hh * sq.gw;
-    } else {
-      trow_t = trow_h = trow_w = sq.table_row + l;
-    }
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      const int pair = dvec * P + j;
-      const int64_t trow = pair < p.tp ? trow_t : (pair < p.thp ? trow_h : trow_w);
-      const float2 c = __ldg(reinterpret_cast<const float2*>(p.cos + trow * p.head_dim + 2 * pair));
-      const float2 sn = __ldg(reinterpret_cast<const float2*>(p.sin + trow * p.head_dim + 2 * pair));
-      ce[j] = c.x;
-      co[j] = c.y;
-      se[j] = sn.x;
-      so[j] = sn.y;
-    }
-  }
-
-  // Row sums of squares (fp32).
   float ssq_q = 0.f, ssq_k = 0.f;
   if (active) {
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float x[E];
-      if (flags & kNormQ) {
-        VT::unpack(qv[i], x);
-#pragma unroll
-        for (int e = 0; e < E; ++e) ssq_q = fmaf(x[e], x[e], ssq_q);
-      }
-      if (flags & kNormK) {
-        VT::unpack(kv[i], x);
-#pragma unroll
-        for (int e = 0; e < E; ++e) ssq_k = fmaf(x[e], x[e], ssq_k);
-      }
+      if (flags & kNormQ) ssq_q += sum_squares<T>(qv[i]);
+      if (flags & kNormK) ssq_k += sum_squares<T>(kv[i]);
     }
   }
-  if (flags & (kNormQ | kNormK)) {
-    for (int o = p.seg >> 1; o > 0; o >>= 1) {
-      ssq_q += __shfl_xor_sync(0xffffffffu, ssq_q, o);
-      ssq_k += __shfl_xor_sync(0xffffffffu, ssq_k, o);
-    }
-    if (p.nseg > 1) {
-      if ((lt % p.seg) == 0) partials[rg * p.nseg + lt / p.seg] = make_float2(ssq_q, ssq_k);
-      __syncthreads();
-      float sum_q = 0.f, sum_k = 0.f;
-      for (int i = 0; i < p.nseg; ++i) {
-        const float2 t = partials[rg * p.nseg + i];
-        sum_q += t.x;
-        sum_k += t.y;
-      }
-      ssq_q = sum_q;
-      ssq_k = sum_k;
-    }
-  }
+  if (flags & (kNormQ | kNormK)) reduce_row(p, partials + rg * p.nseg, lt, ssq_q, ssq_k, [] { __syncthreads(); });
   if (!active) return;
-
-  // rstd = 1 / sqrt(mean(x^2) + eps), each step IEEE-rounded (torch.rsqrt on CPU).
-  const float rstd_q = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssq_q, p.c_f), p.eps)));
-  const float rstd_k = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssq_k, p.c_f), p.eps)));
+  const float rstd_q = rstd_of(ssq_q, p.c_f, p.eps);
+  const float rstd_k = rstd_of(ssq_k, p.c_f, p.eps);
 
   if (flags & kHasQ) {
-    T* qout = static_cast<T*>(p.q_out) + row * p.q_out_stride;
+    T* qout = static_cast<T*>(p.q_out) + t.row * p.q_out_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float x[E], y[E];
+      float x[E];
       VT::unpack(qv[i], x);
-      if (flags & kNormQ) {
-        float w[E];
-        VT::unpack(ld_keep(static_cast<const T*>(p.wq) + elem_off[i]), w);
-#pragma unroll
-        for (int e = 0; e < E; ++e) x[e] = VT::round(__fmul_rn(__fmul_rn(x[e], rstd_q), w[e]));
-      }
-#pragma unroll
-      for (int j = 0; j < P; ++j)
-        rotate_pair(x[2 * j], x[2 * j + 1], ce[j], co[j], se[j], so[j], y[2 * j], y[2 * j + 1]);
-      st_vec(qout + elem_off[i], VT::pack(y));
+      if (flags & kNormQ) normalise<T>(x, ld_keep(static_cast<const T*>(p.wq) + elem_off[i]), rstd_q);
+      st_vec(qout + elem_off[i], rotate<T, P>(x, r));
     }
   }
   if (flags & kHasK) {
-    T* kout = static_cast<T*>(p.k_out) + kv_row * p.k_out_stride;
-    T* kpre = static_cast<T*>(p.k_pre) + row * p.k_pre_stride;
+    T* kout = static_cast<T*>(p.k_out) + t.kv_row * p.k_out_stride;
+    T* kpre = static_cast<T*>(p.k_pre) + t.row * p.k_pre_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float x[E], y[E];
+      float x[E];
       VT::unpack(kv[i], x);
       if (flags & kNormK) {
-        float w[E];
-        VT::unpack(ld_keep(static_cast<const T*>(p.wk) + elem_off[i]), w);
-#pragma unroll
-        for (int e = 0; e < E; ++e) x[e] = VT::round(__fmul_rn(__fmul_rn(x[e], rstd_k), w[e]));
+        normalise<T>(x, ld_keep(static_cast<const T*>(p.wk) + elem_off[i]), rstd_k);
         if (flags & kKPre) st_vec(kpre + elem_off[i], VT::pack(x));
       } else if (flags & kKPre) {
         st_vec(kpre + elem_off[i], kv[i]);
       }
-      if (flags & kKOut) {
-#pragma unroll
-        for (int j = 0; j < P; ++j)
-          rotate_pair(x[2 * j], x[2 * j + 1], ce[j], co[j], se[j], so[j], y[2 * j], y[2 * j + 1]);
-        st_vec(kout + elem_off[i], VT::pack(y));
-      }
+      if (flags & kKOut) st_vec(kout + elem_off[i], rotate<T, P>(x, r));
     }
   }
 }
 
+// ------------------------------------------------------------------------------------
+// bulk_kernel: persistent CTAs, TMA bulk copies through a ring of smem stages
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase of `parity` to complete, giving up after kWaitNs.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - start > kWaitNs) {
+      atomicAdd(&g_wait_timeouts, 1u);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(smem_dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_addr(smem_src)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Per-stage token record written by the producer before it arrives on the stage's
+// full barrier (the arrive releases it to the waiting consumers).
+struct StageMeta {
+  int64_t row;
+  int64_t kv_row;
+  int64_t trow_t, trow_h, trow_w;
+};
+
+// Flag sets with a specialised bulk_kernel (the remaining combinations run the
+// generic instantiation, FLAGS = 0, which reads the flags at run time).
+constexpr int kModeRing = kHasQ | kHasK | kHasV | kNormQ | kNormK | kKOut;  // ring layout prep
+constexpr int kModeRef = kHasQ | kHasK | kNormQ | kNormK | kKPre;           // reference-layout prep
+constexpr int kModeSink = kHasK | kKOut;                                    // sink re-rotation
+
+// bulk_kernel: warp 0 lane 0 is the producer, warp 1 lane 0 drains the V ring,
+// warps 2.. are the consumer row groups.
+//
+// Shared memory (offsets in KParams): full/empty mbarriers of the S q|k stages,
+// vfull/vempty of the SV v stages, per-group abort flags and reduction partials,
+// the StageMeta of every q|k stage and the ring row of every v stage, then the
+// stages.  V rows never wait for q/k compute: they are loaded into their own
+// ring and stored back out by warp 1 as soon as they land, so a q|k stage holds
+// two rows, not three, while it is being computed.
+//
+// The consumer side works on whole rows in shared memory with a runtime loop
+// over its vectors (vector vi = lt + j*tpr of the row), so its registers do not
+// grow with the head count and one or two warps finish a token:
+//   pass 1 -- sum of squares of q and k (packed fp32x2 FMAs);
+//   pass 2 -- y = round((x*rstd)*w), rotated with two packed products and two
+//             scalar adds per pair, written back in place.
+// A thread's vectors all sit at the same head-dim slice (tpr is a multiple of
+// the vectors per head), so its cos/sin pairs are loaded once per token.
+template <typename T, int FLAGS>
+__global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const __grid_constant__ KParams p) {
+  using PT = Pairs16<T>;
+  constexpr int E = Vec16<T>::kElems;
+  constexpr int P = PT::kPairs;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = p.stages;
+  const int SV = p.vstages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  uint64_t* vfull = empty + S;
+  uint64_t* vempty = vfull + SV;
+  int* abort_flag = reinterpret_cast<int*>(smem + p.off_abort);                // [groups]
+  float2* partials_base = reinterpret_cast<float2*>(smem + p.off_partials);    // [groups][nseg]
+  StageMeta* meta = reinterpret_cast<StageMeta*>(smem + p.off_meta);           // [S]
+  int64_t* vmeta = reinterpret_cast<int64_t*>(smem + p.off_vmeta);             // [SV]
+  unsigned char* qk_stages = smem + p.off_stages;
+  unsigned char* v_stages = smem + p.off_vstages;
+
+  const int flags = FLAGS ? FLAGS : p.flags;
+  const bool has_qk = (flags & (kHasQ | kHasK)) != 0;
+  const int G = gridDim.x;
+  const int n_local = p.total > static_cast<int>(blockIdx.x) ? (p.total - 1 - static_cast<int>(blockIdx.x)) / G + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < SV; ++s) {
+      mbar_init(&vfull[s], 1);
+      mbar_init(&vempty[s], 1);
+    }
+    for (int r = 0; r < p.rows; ++r) abort_flag[r] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (threadIdx.x < 32) {
+    // ---------------- producer ----------------
+    if (threadIdx.x == 0) {
+      const T* qb = static_cast<const T*>(p.q);
+      const T* kb = static_cast<const T*>(p.k);
+      const T* vb = static_cast<const T*>(p.v);
+      int issued = 0, vissued = 0;
+      for (int i = 0; i < n_local; ++i) {
+        const int g = static_cast<int>(blockIdx.x) + i * G;
+        const Token t = decode(p, g);
+        if (flags & kHasV) {
+          const int sv = i % SV;
+          if (i >= SV && !mbar_wait(&vempty[sv], ((i / SV) & 1) ^ 1)) break;
+          vmeta[sv] = t.kv_row;
+          mbar_arrive_expect_tx(&vfull[sv], p.row_bytes);
+          bulk_load(v_stages + static_cast<size_t>(sv) * p.vstage_bytes, vb + t.row * p.v_stride, p.row_bytes,
+                    &vfull[sv]);
+          vissued = i + 1;
+        }
+        if (has_qk) {
+          const int s = i % S;
+          if (i >= S && !mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
+          meta[s] = StageMeta{t.row, t.kv_row, t.trow_t, t.trow_h, t.trow_w};
+          unsigned char* st = qk_stages + static_cast<size_t>(s) * p.stage_bytes;
+          mbar_arrive_expect_tx(&full[s], p.load_bytes);
+          if (flags & kHasQ) bulk_load(st, qb + t.row * p.q_stride, p.row_bytes, &full[s]);
+          if (flags & kHasK) bulk_load(st + p.row_bytes, kb + t.row * p.k_stride, p.row_bytes, &full[s]);
+          issued = i + 1;
+        }
+      }
+      // Drain: every load issued must have landed before the CTA may exit.
+      for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
+      for (int i = vissued - SV > 0 ? vissued - SV : 0; i < vissued; ++i) mbar_wait(&vfull[i % SV], (i / SV) & 1);
+    }
+    return;
+  }
+  if (threadIdx.x < 64) {
+    // ---------------- V ring: store each row as soon as it lands ----------------
+    if (threadIdx.x == 32 && (flags & kHasV)) {
+      T* vout = static_cast<T*>(p.v_out);
+      int pending = -1;
+      for (int i = 0; i < n_local; ++i) {
+        const int sv = i % SV;
+        if (!mbar_wait(&vfull[sv], (i / SV) & 1)) break;
+        bulk_store(vout + vmeta[sv] * p.v_out_stride, v_stages + static_cast<size_t>(sv) * p.vstage_bytes,
+                   p.row_bytes);
+        bulk_commit();
+        bulk_wait_read<1>();
+        if (pending >= 0) mbar_arrive(&vempty[pending]);
+        pending = sv;
+      }
+      bulk_wait_read<0>();
+      if (pending >= 0) mbar_arrive(&vempty[pending]);
+      bulk_wait_all();
+    }
+    return;
+  }
+  if (!has_qk) return;
+
+  // ---------------- consumers ----------------
+  const int ct = threadIdx.x - 64;
+  const int rg = ct / p.tpr;
+  const int lt = ct - rg * p.tpr;
+  const int dvec = lt % p.vph;
+  const bool leader = lt == 0;
+  float2* partials = partials_base + rg * p.nseg;
+  volatile int* aborted = abort_flag + rg;
+  const int bar_id = 1 + rg;
+  auto sync = [&] { named_sync(bar_id, p.tpr); };
+  const int nvec = p.C / E;  // 16-byte vectors per row
+  const T* wqb = static_cast<const T*>(p.wq);
+  const T* wkb = static_cast<const T*>(p.wk);
+  int pending = -1;  // leader, deferred release: stage whose stores may still read smem
+
+  for (int i = rg; i < n_local; i += p.rows) {
+    const int s = i % S;
+    if (!mbar_wait(&full[s], (i / S) & 1)) *aborted = 1;
+    const StageMeta t = meta[s];
+    unsigned char* st = qk_stages + static_cast<size_t>(s) * p.stage_bytes;
+    T* sq = reinterpret_cast<T*>(st);
+    T* sk = reinterpret_cast<T*>(st + p.row_bytes);
+
+    // cos / sin of this thread's pairs: (cos[2i], cos[2i+1]) and (sin[2i], sin[2i+1]).
+    f32x2 cc[P], ss[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int pair = dvec * P + j;
+      const int64_t trow = pair < p.tp ? t.trow_t : (pair < p.thp ? t.trow_h : t.trow_w);
+      cc[j] = __ldg(reinterpret_cast<const unsigned long long*>(p.cos + trow * p.head_dim + 2 * pair));
+      ss[j] = __ldg(reinterpret_cast<const unsigned long long*>(p.sin + trow * p.head_dim + 2 * pair));
+    }
+
+    // Pass 1: sums of squares.
+    f32x2 aq0 = 0, aq1 = 0, ak0 = 0, ak1 = 0;
+    if (flags & (kNormQ | kNormK)) {
+#pragma unroll 2
+      for (int vi = lt; vi < nvec; vi += p.tpr) {
+        const int off = vi * E;
+        f32x2 x[P];
+        if (flags & kNormQ) {
+          PT::unpack(*reinterpret_cast<const uint4*>(sq + off), x);
+#pragma unroll
+          for (int j = 0; j < P; j += 2) {
+            aq0 = f2_fma(x[j], x[j], aq0);
+            if (j + 1 < P) aq1 = f2_fma(x[j + 1], x[j + 1], aq1);
+          }
+        }
+        if (flags & kNormK) {
+          PT::unpack(*reinterpret_cast<const uint4*>(sk + off), x);
+#pragma unroll
+          for (int j = 0; j < P; j += 2) {
+            ak0 = f2_fma(x[j], x[j], ak0);
+            if (j + 1 < P) ak1 = f2_fma(x[j + 1], x[j + 1], ak1);
+          }
+        }
+      }
+    }
+    float ssq_q, ssq_k;
+    {
+      float a, b, c, d;
+      f2_split(aq0, a, b);
+      f2_split(aq1, c, d);
+      ssq_q = (a + b) + (c + d);
+      f2_split(ak0, a, b);
+      f2_split(ak1, c, d);
+      ssq_k = (a + b) + (c + d);
+    }
+    if ((flags & (kNormQ | kNormK)) && p.nseg > 1) {
+      reduce_row(p, partials, lt, ssq_q, ssq_k, sync);
+    } else {
+      if (flags & (kNormQ | kNormK)) reduce_row(p, partials, lt, ssq_q, ssq_k, sync);
+      sync();  // orders the abort vote when the reduction needed no barrier
+    }
+    if (*aborted) break;  // every thread of the group passed the same barrier
+    const float rq = rstd_of(ssq_q, p.c_f, p.eps);
+    const float rk = rstd_of(ssq_k, p.c_f, p.eps);
+    const f32x2 rq2 = f2_make(rq, rq), rk2 = f2_make(rk, rk);
+    T* kpre = static_cast<T*>(p.k_pre) + t.row * p.k_pre_stride;
+
+    // Pass 2: normalise, round, rotate, write back in place.
+#pragma unroll 2
+    for (int vi = lt; vi < nvec; vi += p.tpr) {
+      const int off = vi * E;
+      if (flags & kHasQ) {
+        f32x2 x[P], w[P];
+        PT::unpack(*reinterpret_cast<const uint4*>(sq + off), x);
+        if (flags & kNormQ) {
+          PT::unpack(ld_keep(wqb + off), w);
+#pragma unroll
+          for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rq2), w[j]));
+        }
+        float lo[P], hi[P];
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+          float m1e, m1o, m2e, m2o;
+          f2_split(f2_mul(x[j], cc[j]), m1e, m1o);  // (e*ce, o*co)
+          f2_split(f2_mul(x[j], ss[j]), m2e, m2o);  // (e*se, o*so)
+          lo[j] = __fsub_rn(m1e, m2o);              // e*cos[2i] - o*sin[2i+1]
+          hi[j] = __fadd_rn(m1o, m2e);              // o*cos[2i+1] + e*sin[2i]
+        }
+        *reinterpret_cast<uint4*>(sq + off) = PT::pack(lo, hi);
+      }
+      if (flags & kHasK) {
+        f32x2 x[P], w[P];
+        const uint4 raw = *reinterpret_cast<const uint4*>(sk + off);
+        PT::unpack(raw, x);
+        if (flags & kNormK) {
+          PT::unpack(ld_keep(wkb + off), w);
+#pragma unroll
+          for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rk2), w[j]));
+        }
+        if (flags & kKPre) {
+          float lo[P], hi[P];
+#pragma unroll
+          for (int j = 0; j < P; ++j) f2_split(x[j], lo[j], hi[j]);
+          st_vec(kpre + off, (flags & kNormK) ? PT::pack(lo, hi) : raw);
+        }
+        if (flags & kKOut) {
+          float lo[P], hi[P];
+#pragma unroll
+          for (int j = 0; j < P; ++j) {
+            float m1e, m1o, m2e, m2o;
+            f2_split(f2_mul(x[j], cc[j]), m1e, m1o);
+            f2_split(f2_mul(x[j], ss[j]), m2e, m2o);
+            lo[j] = __fsub_rn(m1e, m2o);
+            hi[j] = __fadd_rn(m1o, m2e);
+          }
+          *reinterpret_cast<uint4*>(sk + off) = PT::pack(lo, hi);
+        }
+      }
+    }
+    fence_async_smem();
+    sync();
+    if (leader) {
+      if (flags & kHasQ) bulk_store(static_cast<T*>(p.q_out) + t.row * p.q_out_stride, sq, p.row_bytes);
+      if (flags & kKOut) bulk_store(static_cast<T*>(p.k_out) + t.kv_row * p.k_out_stride, sk, p.row_bytes);
+      bulk_commit();
+      // A stage is free once its stores have read it (the global writes complete
+      // asynchronously).  Deferred: this token's stores stay in flight while the group
+      // computes its next token, and the previous token's stage is freed instead.
+      if (p.defer) {
+        bulk_wait_read<1>();
+        if (pending >= 0) mbar_arrive(&empty[pending]);
+        pending = s;
+      } else {
+        bulk_wait_read<0>();
+        mbar_arrive(&empty[s]);
+      }
+    }
+  }
+  if (leader) {
+    bulk_wait_read<0>();
+    if (pending >= 0) mbar_arrive(&empty[pending]);
+    bulk_wait_all();
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------
 struct Plan {
   KParams params;
+  int kernel;  // PS_KERNEL_ROWS or PS_KERNEL_BULK
   int V;
   int threads;
   int64_t blocks;
@@ -280,15 +719,16 @@ static bool supported_v(int v) { return v == 1 || v == 2 || v == 3 || v == 4 || 
 
 // Chooses heads-per-thread V: prefer V >= 2 with a warp-multiple row group of
 // at most 256 threads (several loads in flight per thread, few registers),
-// then any warp-multiple group, then any group that fits a CTA.
-static int choose_v(int heads, int vph) {
+// then any warp-multiple group, then (rows_kernel only) any group that fits.
+static int choose_v(int heads, int vph, int max_threads, bool warp_multiple) {
   const int order[] = {2, 3, 4, 5, 6, 8, 1};
   for (int v : order)
     if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= 256) return v;
   for (int v : order)
-    if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= kMaxThreads) return v;
+    if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= max_threads) return v;
+  if (warp_multiple) return 0;
   for (int v : order)
-    if (heads % v == 0 && vph * (heads / v) <= kMaxThreads) return v;
+    if (heads % v == 0 && vph * (heads / v) <= max_threads) return v;
   return 0;
 }
 
@@ -304,7 +744,15 @@ static int check_stride(int64_t stride, int64_t C, int es, const char* name) {
   return PS_OK;
 }
 
-static int build_plan(const ps_qk_prep_args* a, Plan* plan) {
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      n > 0)
+    return n;
+  return 148;
+}
+
+static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   clear_error();
   if (!a) return fail(PS_ERR_NULL, "args is NULL");
   if (a->dtype != PS_BF16 && a->dtype != PS_F32) return fail(PS_ERR_DTYPE, "dtype %d is not PS_BF16 or PS_F32", a->dtype);
@@ -313,6 +761,7 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan) {
   if (a->heads < 1 || a->head_dim < 2 || (a->head_dim % 2)) return fail(PS_ERR_SHAPE, "heads=%d head_dim=%d invalid", a->heads, a->head_dim);
   if (a->head_dim % E) return fail(PS_ERR_ALIGN, "head_dim=%d: a head must be whole 16-byte vectors", a->head_dim);
   const int64_t C = static_cast<int64_t>(a->heads) * a->head_dim;
+  if (C > (1 << 20)) return fail(PS_ERR_UNSUPPORTED, "C=%lld too large", (long long)C);
   const int vph = a->head_dim / E;
 
   const bool has_q = a->q != nullptr, has_k = a->k != nullptr, has_v = a->v != nullptr;
@@ -363,47 +812,14 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan) {
   if (a->n_seqs > PS_MAX_SEQS) return fail(PS_ERR_TOO_MANY_SEQS, "n_seqs=%d exceeds PS_MAX_SEQS=%d", a->n_seqs, PS_MAX_SEQS);
   if (!a->seqs) return fail(PS_ERR_NULL, "seqs is NULL");
   if (a->in_rows < 0) return fail(PS_ERR_SHAPE, "in_rows=%lld", (long long)a->in_rows);
-
-  int V = a->heads_per_thread;
-  if (V == 0) V = choose_v(a->heads, vph);
-  if (V <= 0 || a->heads % V) return fail(PS_ERR_UNSUPPORTED, "heads_per_thread=%d does not divide heads=%d", V, a->heads);
-  if (!supported_v(V)) return fail(PS_ERR_UNSUPPORTED, "heads_per_thread=%d not compiled (1,2,3,4,5,6,8)", V);
-  const int tpr = vph * (a->heads / V);
-  if (tpr > kMaxThreads) return fail(PS_ERR_UNSUPPORTED, "row group of %d threads exceeds a CTA", tpr);
-  int rows = tpr >= 256 ? 1 : 256 / tpr;
-  while ((rows * tpr) % 32) ++rows;
-  if (rows * tpr > kMaxThreads) return fail(PS_ERR_UNSUPPORTED, "cannot tile %d-thread rows into whole warps", tpr);
+  if (a->kernel != PS_KERNEL_AUTO && a->kernel != PS_KERNEL_ROWS && a->kernel != PS_KERNEL_BULK)
+    return fail(PS_ERR_SHAPE, "kernel %d unknown", a->kernel);
 
   KParams& k = plan->params;
   memset(&k, 0, sizeof(k));
-  k.q = a->q; k.k = a->k; k.v = a->v; k.wq = norm_q ? a->q_weight : nullptr; k.wk = norm_k ? a->k_weight : nullptr;
-  k.cos = a->cos; k.sin = a->sin;
-  k.q_out = a->q_out; k.k_out = a->k_out; k.v_out = a->v_out; k.k_pre = a->k_pre;
-  k.q_stride = a->q_stride; k.k_stride = a->k_stride; k.v_stride = a->v_stride;
-  k.q_out_stride = a->q_out_stride; k.k_out_stride = a->k_out_stride; k.v_out_stride = a->v_out_stride;
-  k.k_pre_stride = a->k_pre_stride;
-  k.head_dim = a->head_dim;
-  k.C = static_cast<int32_t>(C);
-  k.tpr = tpr;
-  k.rows = rows;
-  k.vph = vph;
-  k.hstep = tpr / vph;
-  k.seg = pow2_segment(tpr);
-  k.nseg = tpr / k.seg;
-  if (a->table_mode == PS_TABLE_AXES) {
-    k.tp = a->t_dim / 2;
-    k.thp = (a->t_dim + a->h_dim) / 2;
-  } else {
-    k.tp = k.thp = a->head_dim;  // every pair reads the token row
-  }
-  k.table_mode = a->table_mode;
   const bool k_out = has_k && a->k_out != nullptr;
   k.flags = (has_q ? kHasQ : 0) | (has_k ? kHasK : 0) | (has_v ? kHasV : 0) | (norm_q ? kNormQ : 0) |
             (norm_k ? kNormK : 0) | (a->k_pre ? kKPre : 0) | (k_out ? kKOut : 0);
-  k.n_seqs = a->n_seqs;
-  k.eps = a->eps;
-  k.c_f = static_cast<float>(C);
-
   int64_t total = 0;
   for (int s = 0; s < a->n_seqs; ++s) {
     const ps_seq& q = a->seqs[s];
@@ -428,7 +844,7 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan) {
                     (long long)(q.table_row + q.n_tokens), (long long)a->table_rows);
       }
     }
-    if (((has_k && a->k_out) || has_v) && q.n_tokens > 0) {
+    if ((k_out || has_v) && q.n_tokens > 0) {
       if (q.ring_frames < 1 || q.ring_slot0 < 0 || q.ring_slot0 >= q.ring_frames)
         return fail(PS_ERR_BOUNDS, "seq %d: ring slot %d outside [0, %d)", s, q.ring_slot0, q.ring_frames);
       if (frames > q.ring_frames)
@@ -438,8 +854,11 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan) {
         return fail(PS_ERR_BOUNDS, "seq %d: ring rows [%lld, %lld) outside kv_out_rows=%lld", s, (long long)q.ring_row,
                     (long long)(q.ring_row + q.ring_frames * hw), (long long)a->kv_out_rows);
     }
+    if (q.n_tokens >= (1 << 30)) return fail(PS_ERR_UNSUPPORTED, "seq %d: sizes beyond 2^30 tokens", s);
     k.cum[s] = static_cast<int32_t>(total);
     DevSeq& d = k.seq[s];
+    d.hw_magic = div_magic(static_cast<uint32_t>(hw));
+    d.gw_magic = div_magic(static_cast<uint32_t>(q.grid_w));
     d.row0 = q.token_start;
     d.table_row = q.table_row;
     d.ring_row = q.ring_row;
@@ -449,32 +868,182 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan) {
     d.ring_frames = q.ring_frames > 0 ? q.ring_frames : 1;
     d.ring_slot0 = q.ring_slot0;
     total += q.n_tokens;
-    if (total > INT32_MAX) return fail(PS_ERR_SHAPE, "more than 2^31-1 tokens in one call");
+    if (total > (1 << 30)) return fail(PS_ERR_SHAPE, "more than 2^30 tokens in one call");
   }
   k.cum[a->n_seqs] = static_cast<int32_t>(total);
   k.total = static_cast<int32_t>(total);
+  k.n_seqs = a->n_seqs;
 
-  plan->V = V;
-  plan->threads = rows * tpr;
-  plan->blocks = (total + rows - 1) / rows;
-  plan->smem = k.nseg > 1 ? static_cast<size_t>(rows) * k.nseg * sizeof(float2) : 0;
+  // Kernel and tiling.
+  const int row_bytes = static_cast<int>(C * es);
+  const int qk_stage_bytes = (2 * row_bytes + 127) & ~127;
+  const int v_stage_bytes = (row_bytes + 127) & ~127;
+  const int nvec = static_cast<int>(C / E);
+  const bool bulk_shape =
+      (32 % vph) == 0 && 2048 + 4 * qk_stage_bytes + 2 * v_stage_bytes <= kBulkSmemBudget;
+  int kernel = a->kernel;
+  if (kernel == PS_KERNEL_AUTO) kernel = bulk_shape ? PS_KERNEL_BULK : PS_KERNEL_ROWS;
+  if (a->release < 0 || a->release > 2) return fail(PS_ERR_SHAPE, "release mode %d unknown", a->release);
+  if (a->reserved1 != 0) return fail(PS_ERR_SHAPE, "reserved1 must be 0");
+
+  k.q = a->q; k.k = a->k; k.v = a->v; k.wq = norm_q ? a->q_weight : nullptr; k.wk = norm_k ? a->k_weight : nullptr;
+  k.cos = a->cos; k.sin = a->sin;
+  k.q_out = a->q_out; k.k_out = a->k_out; k.v_out = a->v_out; k.k_pre = a->k_pre;
+  k.q_stride = a->q_stride; k.k_stride = a->k_stride; k.v_stride = a->v_stride;
+  k.q_out_stride = a->q_out_stride; k.k_out_stride = a->k_out_stride; k.v_out_stride = a->v_out_stride;
+  k.k_pre_stride = a->k_pre_stride;
+  k.head_dim = a->head_dim;
+  k.C = static_cast<int32_t>(C);
+  k.vph = vph;
+  if (a->table_mode == PS_TABLE_AXES) {
+    k.tp = a->t_dim / 2;
+    k.thp = (a->t_dim + a->h_dim) / 2;
+  } else {
+    k.tp = k.thp = a->head_dim;  // every pair reads the token row
+  }
+  k.table_mode = a->table_mode;
+  k.eps = a->eps;
+  k.c_f = static_cast<float>(C);
+  plan->kernel = kernel;
   plan->elem_size = es;
+
+  if (kernel == PS_KERNEL_ROWS) {
+    int V = a->heads_per_thread;
+    if (V == 0) V = choose_v(a->heads, vph, kMaxThreads, false);
+    if (V <= 0 || a->heads % V) return fail(PS_ERR_UNSUPPORTED, "heads_per_thread=%d does not divide heads=%d", V, a->heads);
+    if (!supported_v(V)) return fail(PS_ERR_UNSUPPORTED, "heads_per_thread=%d not compiled (1,2,3,4,5,6,8)", V);
+    const int tpr = vph * (a->heads / V);
+    if (tpr > kMaxThreads) return fail(PS_ERR_UNSUPPORTED, "row group of %d threads exceeds a CTA", tpr);
+    int rows = tpr >= 256 ? 1 : 256 / tpr;
+    while ((rows * tpr) % 32) ++rows;
+    if (rows * tpr > kMaxThreads) return fail(PS_ERR_UNSUPPORTED, "cannot tile %d-thread rows into whole warps", tpr);
+    k.tpr = tpr;
+    k.hstep = tpr / vph;
+    k.seg = pow2_segment(tpr);
+    k.nseg = tpr / k.seg;
+    k.rows = rows;
+    plan->V = V;
+    plan->threads = rows * tpr;
+    plan->blocks = (total + rows - 1) / rows;
+    plan->smem = k.nseg > 1 ? static_cast<size_t>(rows) * k.nseg * sizeof(float2) : 0;
+    return PS_OK;
+  }
+
+  // Bulk kernel.  A row group of tpr threads (whole warps; named barriers count
+  // warps) owns a token; thread lt covers vectors lt, lt + tpr, ... of the row, all
+  // at head-dim slice lt % vph, which needs tpr to be a multiple of vph.
+  if ((32 % vph) != 0)
+    return fail(PS_ERR_UNSUPPORTED, "bulk kernel needs the vectors of a head (%d) to divide a warp", vph);
+  int tpr = a->row_threads;
+  if (tpr == 0) tpr = nvec >= 512 ? 64 : 32;
+  if (tpr < 32 || tpr % 32 || tpr > kBulkMaxConsumers)
+    return fail(PS_ERR_UNSUPPORTED, "row_threads=%d must be a multiple of 32 up to %d", tpr, kBulkMaxConsumers);
+  k.tpr = tpr;
+  k.hstep = 0;
+  k.seg = 32;
+  k.nseg = tpr / 32;
+  // Shared memory: V stages take about a quarter of the budget (they are short-lived),
+  // q|k stages the rest.
+  int vstages = has_v ? (a->vstages > 0 ? a->vstages : kBulkSmemBudget / 4 / v_stage_bytes) : 0;
+  if (has_v && vstages < 2) vstages = 2;
+  if (vstages > 32) vstages = 32;
+  auto header = [&](int S, int SV, int groups) {
+    int off = 16 * S + 16 * SV;         // mbarriers
+    off += 64;                          // abort flags
+    off += 8 * groups * k.nseg;         // partials
+    off += static_cast<int>(sizeof(StageMeta)) * S + 8 * SV;
+    return (off + 127) & ~127;
+  };
+  int groups = a->groups;
+  const int room = kBulkSmemBudget - vstages * v_stage_bytes - header(64, vstages, kBulkMaxGroups);
+  const int max_stages_fit = room / qk_stage_bytes;
+  if (groups <= 0) {
+    // Six row groups measured best on B200 for C = 1536 .. 5120 (one token in flight
+    // per group; more groups only add stages held by compute).
+    groups = 6;
+    if (groups > max_stages_fit - 2) groups = max_stages_fit - 2;
+    if (groups < 1) groups = 1;
+  }
+  if (groups > kBulkMaxGroups) groups = kBulkMaxGroups;
+  while (groups > 1 && groups * tpr > kBulkMaxConsumers) --groups;
+  int stages = a->stages;
+  if (stages <= 0) stages = (kBulkSmemBudget - vstages * v_stage_bytes - header(64, vstages, groups)) / qk_stage_bytes;
+  if (stages > 64) stages = 64;
+  const int head = header(stages, vstages, groups);
+  const size_t layout = static_cast<size_t>(head) + static_cast<size_t>(stages) * qk_stage_bytes +
+                        static_cast<size_t>(vstages) * v_stage_bytes;
+  const bool defer = a->release == 2 || (a->release == 0 && stages >= 2 * groups + 2);
+  if (stages < (defer ? 2 * groups + 1 : groups + 1) || layout > static_cast<size_t>(kBulkSmemBudget))
+    return fail(PS_ERR_UNSUPPORTED, "%d stages of %d bytes for %d row groups do not fit shared memory", stages,
+                qk_stage_bytes, groups);
+  k.defer = defer ? 1 : 0;
+  k.rows = groups;
+  k.stages = stages;
+  k.vstages = vstages;  // 0 without a V role
+  k.row_bytes = row_bytes;
+  k.stage_bytes = qk_stage_bytes;
+  k.vstage_bytes = v_stage_bytes;
+  k.load_bytes = row_bytes * ((has_q ? 1 : 0) + (has_k ? 1 : 0));
+  k.off_abort = 16 * stages + 16 * vstages;
+  k.off_partials = k.off_abort + 64;
+  k.off_meta = k.off_partials + 8 * groups * k.nseg;
+  k.off_vmeta = k.off_meta + static_cast<int>(sizeof(StageMeta)) * stages;
+  k.off_stages = head;
+  k.off_vstages = head + stages * qk_stage_bytes;
+  plan->V = 0;
+  plan->threads = 64 + groups * tpr;
+  plan->smem = layout;
+  int ctas = host_only ? 148 : sm_count();
+  if (a->ctas_per_sm > 1) ctas *= a->ctas_per_sm;
+  plan->blocks = total < ctas ? total : ctas;
   return PS_OK;
+}
+
+// Opts a bulk_kernel instantiation into its dynamic shared memory once per device.
+static cudaError_t allow_smem(const void* fn, int bytes) {
+  struct Entry {
+    const void* fn;
+    int device;
+    int bytes;
+  };
+  static Entry cache[64];
+  static int used = 0;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].device == dev && cache[i].bytes >= bytes) return cudaSuccess;
+  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess && used < 64) cache[used++] = Entry{fn, dev, bytes};
+  return err;
 }
 
 template <typename T>
 static cudaError_t launch_typed(const Plan& plan, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(plan.blocks)), block(plan.threads);
-  switch (plan.V) {
-    case 1: qk_prep_kernel<T, 1><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 2: qk_prep_kernel<T, 2><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 3: qk_prep_kernel<T, 3><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 4: qk_prep_kernel<T, 4><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 5: qk_prep_kernel<T, 5><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 6: qk_prep_kernel<T, 6><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 8: qk_prep_kernel<T, 8><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    default: return cudaErrorInvalidValue;
+  if (plan.kernel == PS_KERNEL_ROWS) {
+    switch (plan.V) {
+      case 1: rows_kernel<T, 1><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      case 2: rows_kernel<T, 2><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      case 3: rows_kernel<T, 3><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      case 4: rows_kernel<T, 4><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      case 5: rows_kernel<T, 5><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      case 6: rows_kernel<T, 6><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      case 8: rows_kernel<T, 8><<<grid, block, plan.smem, stream>>>(plan.params); break;
+      default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
   }
+  void (*fn)(KParams) = bulk_kernel<T, 0>;
+  switch (plan.params.flags) {
+    case kModeRing: fn = bulk_kernel<T, kModeRing>; break;
+    case kModeRef: fn = bulk_kernel<T, kModeRef>; break;
+    case kModeSink: fn = bulk_kernel<T, kModeSink>; break;
+    default: break;
+  }
+  cudaError_t err = allow_smem(reinterpret_cast<const void*>(fn), static_cast<int>(plan.smem));
+  if (err != cudaSuccess) return err;
+  fn<<<grid, block, plan.smem, stream>>>(plan.params);
   return cudaGetLastError();
 }
 
@@ -483,12 +1052,12 @@ static cudaError_t launch_typed(const Plan& plan, cudaStream_t stream) {
 
 extern "C" int32_t ps_qk_prep_validate(const ps_qk_prep_args* args) {
   ps::Plan plan;
-  return ps::build_plan(args, &plan);
+  return ps::build_plan(args, &plan, true);
 }
 
 extern "C" int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream) {
   ps::Plan plan;
-  const int rc = ps::build_plan(args, &plan);
+  const int rc = ps::build_plan(args, &plan, false);
   if (rc != PS_OK) return rc;
   if (plan.blocks == 0) return PS_OK;
   if (plan.blocks > 0x7fffffffLL) return ps::fail(PS_ERR_UNSUPPORTED, "grid of %lld CTAs", (long long)plan.blocks);
@@ -496,5 +1065,18 @@ extern "C" int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream)
                               ? ps::launch_typed<__nv_bfloat16>(plan, static_cast<cudaStream_t>(stream))
                               : ps::launch_typed<float>(plan, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "qk_prep launch: %s", cudaGetErrorString(err));
+  return PS_OK;
+}
+
+extern "C" int32_t ps_device_timeouts(uint32_t* count, int32_t reset) {
+  ps::clear_error();
+  if (!count) return ps::fail(PS_ERR_NULL, "count is NULL");
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err == cudaSuccess) err = cudaMemcpyFromSymbol(count, ps::g_wait_timeouts, sizeof(uint32_t));
+  if (err == cudaSuccess && reset) {
+    const uint32_t zero = 0;
+    err = cudaMemcpyToSymbol(ps::g_wait_timeouts, &zero, sizeof(uint32_t));
+  }
+  if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "reading the timeout counter: %s", cudaGetErrorString(err));
   return PS_OK;
 }

@@ -72,16 +72,15 @@ def rope(x: torch.Tensor, cosine: torch.Tensor, sine: torch.Tensor, out: torch.T
             raise PrepError(f"{name} must be float32 (the reference's tables are fp32)")
         if t.dim() != 4 or t.shape[1] != L or t.shape[2] != 1 or t.shape[3] != D or t.shape[0] not in (1, B):
             raise PrepError(f"{name} must be [B or 1, {L}, 1, {D}], got {tuple(t.shape)}")
-    if cosine.stride() != sine.stride():
-        sine = sine.contiguous() if sine.stride() != cosine.contiguous().stride() else sine
-        cosine = cosine.contiguous()
-    if cosine.stride(3) != 1:
+    if cosine.stride() != sine.stride() or cosine.stride(3) != 1:
         cosine, sine = cosine.contiguous(), sine.contiguous()
     if out is None:
         out = torch.empty_like(x)
     elif out.shape != x.shape or out.dtype != x.dtype:
         raise PrepError("out must match x in shape and dtype")
     device = _require_cuda(x, cosine, sine, out)
+    if x.numel() == 0:
+        return out
     if x.stride(3) != 1 or out.stride(3) != 1:
         raise PrepError("x and out need a unit stride on the head dimension")
     tab_batch = 0 if cosine.shape[0] == 1 else cosine.stride(0)
@@ -167,6 +166,13 @@ def qk_norm_rope_kv(
     table_mode: str = "axes",
     axis_split: Sequence[int] | None = None,
     heads_per_thread: int = 0,
+    kernel: str = "auto",
+    stages: int = 0,
+    groups: int = 0,
+    ctas_per_sm: int = 0,
+    row_threads: int = 0,
+    release: int = 0,
+    vstages: int = 0,
 ) -> None:
     """One fused launch (per ``PS_MAX_SEQS`` sequences) of ``ps_qk_norm_rope_kv``.
 
@@ -175,6 +181,9 @@ def qk_norm_rope_kv(
     (``cos``/``sin`` are the [max_len, D] per-axis tables, positions decoded from each
     sequence's grid and frame offset) or "tokens" (``cos``/``sin`` are per-token rows,
     [rows, D] or the reference's [B, L, 1, D] tables, read at ``table_row + l``).
+    ``kernel`` is "auto", "bulk" (persistent cp.async.bulk pipeline) or "rows"; the tiling
+    knobs (``heads_per_thread`` for rows; ``row_threads``, ``stages``, ``groups``,
+    ``ctas_per_sm``, ``release``, ``vstages`` for bulk) default to the library's choice.
     """
     C = heads * head_dim
     ref = next(t for t in (q, k, v) if t is not None)
@@ -221,7 +230,8 @@ def qk_norm_rope_kv(
         args = _lib.PsQkPrepArgs(
             dtype=dtype, heads=heads, head_dim=head_dim, table_mode=mode,
             t_dim=split[0], h_dim=split[1], w_dim=split[2], n_seqs=len(part), eps=float(eps),
-            heads_per_thread=heads_per_thread, in_rows=in_rows,
+            heads_per_thread=heads_per_thread, kernel=_KERNELS[kernel], stages=stages, groups=groups,
+            ctas_per_sm=ctas_per_sm, row_threads=row_threads, release=release, vstages=vstages, in_rows=in_rows,
             q=qp, q_stride=qs, k=kp, k_stride=ks, v=vp, v_stride=vs,
             q_weight=None if q_weight is None else q_weight.data_ptr(),
             k_weight=None if k_weight is None else k_weight.data_ptr(),
@@ -230,6 +240,16 @@ def qk_norm_rope_kv(
             kv_out_rows=kv_rows, k_pre=kpp, k_pre_stride=kps,
             seqs=ctypes.cast(array, ctypes.POINTER(_lib.PsSeq)))
         _check(lib.ps_qk_norm_rope_kv(ctypes.byref(args), stream))
+
+
+_KERNELS = {"auto": _lib.KERNEL_AUTO, "rows": _lib.KERNEL_ROWS, "bulk": _lib.KERNEL_BULK}
+
+
+def device_timeouts(reset: bool = True) -> int:
+    """Bounded waits of the bulk kernel that ran out on the current device (synchronises)."""
+    count = ctypes.c_uint32(0)
+    _check(_lib.load().ps_device_timeouts(ctypes.byref(count), int(reset)))
+    return int(count.value)
 
 
 def _default_split(head_dim: int) -> tuple[int, int, int]:

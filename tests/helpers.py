@@ -9,6 +9,12 @@ fp32 oracle <= 2^-7 relative; cache slot indexing bit-exact):
 * RMSNorm: the kernel's fp32 row sum runs in a different order than torch's CPU sum, so
   a value lying within ~1e-7 of a bf16 rounding boundary may round the other way: every
   output is within ONE bf16 ulp of the reference, and at most 1e-3 of them differ at all.
+* Rotated Q/K against the reference's bf16 path: identical wherever the RMSNorm outputs
+  agree (checked exactly for K through the kernel's own normalised K).  Where one input
+  of a pair is one ulp apart, e*c - o*s moves by at most one ulp of the pair magnitude
+  r = |(e, o)| (plus the two output roundings), which for a near-zero output is many
+  ulps of the output itself: the bound is |got - ref| <= 2^-6 * r, and at most 1e-3 of
+  the elements differ at all.
 * Against the fp64 evaluation of the reference's formulas: max-abs error <= 2^-7 x
   max|reference| over the tensor, and per element <= 2^-6 x the magnitude of its pair.
 """
@@ -43,6 +49,19 @@ def check_bf16_close(got: torch.Tensor, want: torch.Tensor, what: str, max_fract
     worst = int(ulps.max()) if ulps.numel() else 0
     fraction = float((ulps > 0).float().mean()) if ulps.numel() else 0.0
     assert worst <= MAX_ULPS, f"{what}: {worst} bf16 ulps"
+    assert fraction <= max_fraction, f"{what}: {fraction:.2e} of elements differ"
+    return worst, fraction
+
+
+def check_rotated_close(got: torch.Tensor, want: torch.Tensor, normed: torch.Tensor, what: str,
+                        max_fraction=ULP_MISMATCH_FRACTION):
+    """Rotated outputs vs the reference's bf16 path: |diff| <= 2^-6 |pair|, few elements differing."""
+    got = got.detach().cpu()
+    diff = (got.double() - want.double()).abs()
+    bound = PAIR_REL * pair_magnitude(normed)
+    fraction = float((diff > 0).float().mean()) if diff.numel() else 0.0
+    worst = float((diff / bound.clamp_min(1e-30)).max()) if diff.numel() else 0.0
+    assert bool((diff <= bound + 1e-30).all()), f"{what}: {worst:.2f} x the 2^-6 pair bound"
     assert fraction <= max_fraction, f"{what}: {fraction:.2e} of elements differ"
     return worst, fraction
 

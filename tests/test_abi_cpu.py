@@ -111,9 +111,15 @@ def test_validate_accepts_config2(lib):
     (dict(in_rows=1000), _lib.ERR_BOUNDS, "in_rows"),
     (dict(q=None, k=None, v=None), _lib.ERR_NULL, "all NULL"),
     (dict(k_out=None), _lib.ERR_NULL, "k given without k_out or k_pre"),
-    (dict(heads_per_thread=5), _lib.ERR_UNSUPPORTED, "does not divide"),
-    (dict(heads_per_thread=7, heads=7, seqs=[_lib.PsSeq(0, 1560, 30, 52, 3, 0, 0, 12, 3)]), _lib.ERR_UNSUPPORTED,
-     "not compiled"),
+    (dict(kernel=_lib.KERNEL_ROWS, heads_per_thread=5), _lib.ERR_UNSUPPORTED, "does not divide"),
+    (dict(kernel=_lib.KERNEL_ROWS, heads_per_thread=7, heads=7, seqs=[_lib.PsSeq(0, 1560, 30, 52, 3, 0, 0, 12, 3)]),
+     _lib.ERR_UNSUPPORTED, "not compiled"),
+    (dict(kernel=_lib.KERNEL_BULK, row_threads=48), _lib.ERR_UNSUPPORTED, "multiple of 32"),
+    (dict(kernel=_lib.KERNEL_BULK, groups=4, stages=3), _lib.ERR_UNSUPPORTED, "do not fit"),
+    (dict(kernel=9), _lib.ERR_SHAPE, "kernel 9 unknown"),
+    (dict(release=3), _lib.ERR_SHAPE, "release mode 3 unknown"),
+    (dict(reserved1=1), _lib.ERR_SHAPE, "reserved1"),
+    (dict(kernel=_lib.KERNEL_BULK, release=2, groups=3, stages=6), _lib.ERR_UNSUPPORTED, "do not fit"),
 ])
 def test_validate_rejects(lib, over, status, text):
     got, message = _validate(lib, _args(**over))

@@ -10,8 +10,8 @@ from physisserve_b200 import ops
 from physisserve_b200.ops import Seq, qk_norm_rope_kv
 from physisserve_b200.wan import Attention, RingCache, prep_ring, prepare_reference_layout, rope, window_layout
 
-from helpers import (check_against_exact, check_bf16_close, exact_prep, norm_weight, pair_magnitude, randn,
-                      token_tables)
+from helpers import (check_against_exact, check_bf16_close, check_rotated_close, exact_prep, norm_weight,
+                     pair_magnitude, randn, token_tables)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -55,7 +55,7 @@ def test_rope_empty_input():
 # Fused RMSNorm + RoPE + ring write
 # ---------------------------------------------------------------------------------------
 def _run_ring(q, k, v, wq, wk, cos, sin, split, grid, offsets, capacity, slots, heads, head_dim, dtype=torch.bfloat16,
-              k_pre=False, heads_per_thread=0):
+              k_pre=False, heads_per_thread=0, kernel="auto", **tiling):
     """One fused launch for B streams of one chunk each; returns GPU (q_out, ring_k, ring_v, k_pre)."""
     B, L, C = q.shape
     gh, gw = grid
@@ -70,7 +70,8 @@ def _run_ring(q, k, v, wq, wk, cos, sin, split, grid, offsets, capacity, slots, 
             for b in range(B)]
     qk_norm_rope_kv(heads=heads, head_dim=head_dim, seqs=seqs, cos=cos.to(DEV), sin=sin.to(DEV), q=dq, k=dk, v=dv,
                     q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v,
-                    k_pre=pre, table_mode="axes", axis_split=split, heads_per_thread=heads_per_thread)
+                    k_pre=pre, table_mode="axes", axis_split=split, heads_per_thread=heads_per_thread, kernel=kernel,
+                    **tiling)
     torch.cuda.synchronize()
     return q_out.cpu(), ring_k.view(B, rows, C).cpu(), ring_v.view(B, rows, C).cpu(), (pre.cpu() if k_pre else None)
 
@@ -82,38 +83,51 @@ def _check_streams(q, k, v, wq, wk, cos, sin, split, grid, offsets, capacity, sl
     gh, gw = grid
     hw = gh * gw
     frames = L // hw
-    ref_k = torch.zeros_like(ring_k)
-    ref_v = torch.zeros_like(ring_v)
-    ref_q = oracle.prep_ring(q, k, v, wq, wk, EPS, cos, sin, split, gh, gw, offsets, ref_k, ref_v, slots)
-    stats = {}
-    stats["q"] = check_bf16_close(q_out, ref_q, "rotated Q")
-    # Ring rows: V bit-exact at the right slots; K within tolerance there; untouched slots still zero.
-    assert torch.equal(ring_v, ref_v), "V ring rows / slot indexing"
-    stats["k"] = check_bf16_close(ring_k, ref_k, "rotated K ring")
-    written = torch.zeros(B, capacity * hw, dtype=torch.bool)
+    stats = {"q": [], "k": [], "q_rel": [], "k_pre": []}
     for b in range(B):
+        sl = slice(b, b + 1)
+        ref_k = torch.zeros_like(ring_k[sl])
+        ref_v = torch.zeros_like(ring_v[sl])
+        ref_q = oracle.prep_ring(q[sl], k[sl], v[sl], wq, wk, EPS, cos, sin, split, gh, gw, offsets[sl], ref_k, ref_v,
+                                 slots[sl])
+        stats["q"].append(check_rotated_close(q_out[sl], ref_q, oracle.rms_norm(q[sl], wq, EPS),
+                                              f"rotated Q stream {b}"))
+        # Ring rows: V bit-exact at the right slots, K within tolerance, untouched slots still zero.
+        assert torch.equal(ring_v[sl], ref_v), f"V ring rows / slot indexing, stream {b}"
+        stats["k"].append(check_rotated_close(ring_k[sl], ref_k, _ring_normed(k[sl], wk, slots[b], capacity, hw,
+                                                                              frames), f"rotated K ring stream {b}"))
+        written = torch.zeros(capacity * hw, dtype=torch.bool)
         for f in range(frames):
             slot = (slots[b] + f) % capacity
-            written[b, slot * hw:(slot + 1) * hw] = True
-    assert torch.equal(ring_k[~written], torch.zeros_like(ring_k[~written]))
-    # fp64 yardstick.
-    for b in range(B):
+            written[slot * hw:(slot + 1) * hw] = True
+        assert not bool(ring_k[b][~written].any()), f"stream {b} wrote outside its slots"
         ct, st = token_tables(cos, sin, split, offsets[b], frames, gh, gw)
         exact_q, normed_q = exact_prep(q[b], wq, EPS, ct, st, heads)
-        stats.setdefault("q_rel", []).append(check_against_exact(q_out[b], exact_q, pair_magnitude(normed_q), "Q"))
-    if k_pre is not None:
-        # RoPE and slot placement exactly reproduced from the kernel's own RMSNorm output.
-        stats["k_pre"] = check_bf16_close(k_pre, oracle.rms_norm(k, wk, EPS), "normalised K")
-        recomputed_k = torch.zeros_like(ring_k)
-        scratch_v = torch.zeros_like(ring_v)
-        oracle.prep_ring(k_pre, k_pre, v, wq, wk, EPS, cos, sin, split, gh, gw, offsets, recomputed_k, scratch_v, slots,
-                         norm=False)
-        assert torch.equal(ring_k, recomputed_k), "RoPE of the kernel's normalised K is not bit-exact"
+        stats["q_rel"].append(check_against_exact(q_out[b], exact_q, pair_magnitude(normed_q), "Q"))
+        if k_pre is not None:
+            # RoPE and slot placement exactly reproduced from the kernel's own RMSNorm output.
+            stats["k_pre"].append(check_bf16_close(k_pre[sl], oracle.rms_norm(k[sl], wk, EPS), "normalised K"))
+            recomputed_k = torch.zeros_like(ref_k)
+            scratch_v = torch.zeros_like(ref_v)
+            oracle.prep_ring(k_pre[sl], k_pre[sl], v[sl], wq, wk, EPS, cos, sin, split, gh, gw, offsets[sl],
+                             recomputed_k, scratch_v, slots[sl], norm=False)
+            assert torch.equal(ring_k[sl], recomputed_k), "RoPE of the kernel's normalised K is not bit-exact"
     return stats
 
 
-@pytest.mark.parametrize("heads_per_thread", [0, 1, 2, 3, 4, 6])
-def test_fused_small_bit_exact_rope_and_slots(heads_per_thread):
+def _ring_normed(k, wk, slot0, capacity, hw, frames):
+    """The reference's normalised K placed at the ring rows its rotated values occupy."""
+    normed = oracle.rms_norm(k, wk, EPS)[0]
+    out = torch.zeros(1, capacity * hw, normed.shape[-1], dtype=normed.dtype)
+    for f in range(frames):
+        slot = (slot0 + f) % capacity
+        out[0, slot * hw:(slot + 1) * hw] = normed[f * hw:(f + 1) * hw]
+    return out
+
+
+@pytest.mark.parametrize("kernel,tile", [("rows", v) for v in (0, 1, 2, 3, 4, 6)] +
+                         [("bulk", t) for t in (0, 32, 64, 96, 128, 192)])
+def test_fused_small_bit_exact_rope_and_slots(kernel, tile):
     H, D, gh, gw = 12, 128, 6, 8
     C = H * D
     B, frames, capacity = 3, 2, 5
@@ -123,8 +137,29 @@ def test_fused_small_bit_exact_rope_and_slots(heads_per_thread):
     cos, sin = oracle.rope_tables(D, 64)
     split = oracle.axis_dims(D)
     offsets, slots = [3, 17, 40], [4, 0, 2]
+    tiling = dict(heads_per_thread=tile) if kernel == "rows" else dict(row_threads=tile)
     got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True,
-                    heads_per_thread=heads_per_thread)
+                    kernel=kernel, **tiling)
+    _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
+
+
+@pytest.mark.parametrize("stages,groups,ctas,release,vstages", [
+    (3, 1, 1, 1, 2), (4, 2, 1, 1, 3), (9, 4, 2, 2, 0), (0, 0, 1, 0, 0), (5, 3, 1, 1, 2), (3, 1, 1, 2, 5),
+    (7, 3, 1, 2, 16)])
+def test_bulk_pipeline_shapes(stages, groups, ctas, release, vstages):
+    """The bulk kernel over few / many stages and row groups, with more tokens than CTAs so
+    every stage is reused many times (exercises the full/empty mbarrier phases)."""
+    H, D, gh, gw = 12, 128, 5, 7
+    C = H * D
+    B, frames, capacity = 4, 3, 4
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s) for s in (71, 72, 73))
+    wq, wk = norm_weight(C, 74), norm_weight(C, 75)
+    cos, sin = oracle.rope_tables(D, 64)
+    split = oracle.axis_dims(D)
+    offsets, slots = [3, 9, 20, 31], [1, 0, 3, 2]
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True,
+                    kernel="bulk", stages=stages, groups=groups, ctas_per_sm=ctas, release=release, vstages=vstages)
     _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
 
 
@@ -155,6 +190,7 @@ def test_config2_steady_state_ring_of_12():
     ref_k = torch.zeros(1, capacity * hw, C, dtype=torch.bfloat16)
     ref_v = torch.zeros_like(ref_k)
     dcos, dsin, dwq, dwk = cos.to(DEV), sin.to(DEV), wq.to(DEV), wk.to(DEV)
+    normed_ring = torch.zeros(capacity * hw, C, dtype=torch.bfloat16)
     for offset in range(3, 21):
         q, k, v = (randn((1, hw, C), 100 * offset + s) for s in range(3))
         slot = ops.ring_slot(offset, capacity)
@@ -164,10 +200,11 @@ def test_config2_steady_state_ring_of_12():
                         sin=dsin, q=q[0].to(DEV), k=k[0].to(DEV), v=v[0].to(DEV), q_weight=dwq, k_weight=dwk,
                         eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v, table_mode="axes")
         ref_q = oracle.prep_ring(q, k, v, wq, wk, EPS, cos, sin, split, gh, gw, [offset], ref_k, ref_v, [slot])
-        check_bf16_close(q_out.cpu(), ref_q[0], f"Q at offset {offset}")
+        check_rotated_close(q_out.cpu(), ref_q[0], oracle.rms_norm(q[0], wq, EPS), f"Q at offset {offset}")
+        normed_ring[slot * hw:(slot + 1) * hw] = oracle.rms_norm(k[0], wk, EPS)
     torch.cuda.synchronize()
     assert torch.equal(ring_v.cpu(), ref_v[0])
-    check_bf16_close(ring_k.cpu(), ref_k[0], "K ring after 18 chunks")
+    check_rotated_close(ring_k.cpu(), ref_k[0], normed_ring, "K ring after 18 chunks")
     # Slot s holds the chunk whose offset is the largest offset <= 20 with offset % 12 == s.
     for s in range(capacity):
         offset = max(o for o in range(3, 21) if o % 12 == s)
@@ -175,7 +212,8 @@ def test_config2_steady_state_ring_of_12():
         assert torch.equal(ring_v[s * hw:(s + 1) * hw].cpu(), v_expected), s
 
 
-def test_config3_batched_14b():
+@pytest.mark.parametrize("kernel", ["bulk", "rows"])
+def test_config3_batched_14b(kernel):
     """8 streams [8, 1560, 40, 128], offsets U{3..40}, per-stream ring of 12."""
     H, D, gh, gw, capacity = 40, 128, 30, 52, 12
     C, hw, B = H * D, 30 * 52, 8
@@ -186,12 +224,14 @@ def test_config3_batched_14b():
     wq, wk = norm_weight(C, 34), norm_weight(C, 35)
     cos, sin = oracle.rope_tables(D, 1024)
     split = oracle.axis_dims(D)
-    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True)
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True,
+                    kernel=kernel)
     stats = _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
-    print("config3 parity", stats)
+    print("config3 parity", kernel, stats)
 
 
-def test_config4_varlen_mixed_chunks():
+@pytest.mark.parametrize("kernel", ["bulk", "rows"])
+def test_config4_varlen_mixed_chunks(kernel):
     """16 streams packed varlen -- 4 first chunks (3x22x40) and 12 steady
     chunks (1x22x40), H=24, C=3072 -- each into its own ring of 12 frames."""
     H, D, gh, gw, capacity = 24, 128, 22, 40, 12
@@ -220,7 +260,8 @@ def test_config4_varlen_mixed_chunks():
     ring_k = torch.zeros(16 * rows, C, device=DEV, dtype=torch.bfloat16)
     ring_v = torch.zeros_like(ring_k)
     qk_norm_rope_kv(heads=H, head_dim=D, seqs=seqs, cos=cos.to(DEV), sin=sin.to(DEV), q=dq, k=dk, v=dv,
-                    q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v)
+                    q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v,
+                    kernel=kernel)
     torch.cuda.synchronize()
     q_out, ring_k, ring_v = q_out.cpu(), ring_k.view(16, rows, C).cpu(), ring_v.view(16, rows, C).cpu()
     for n, i in enumerate(order):
@@ -229,12 +270,14 @@ def test_config4_varlen_mixed_chunks():
         ref_v = torch.zeros_like(ref_k)
         ref_q = oracle.prep_ring(q[None, sl], k[None, sl], v[None, sl], wq, wk, EPS, cos, sin, split, gh, gw,
                                  [offsets[i]], ref_k, ref_v, [offsets[i] % capacity])
-        check_bf16_close(q_out[sl], ref_q[0], f"Q member {i}")
-        check_bf16_close(ring_k[i], ref_k[0], f"K member {i}")
+        check_rotated_close(q_out[sl], ref_q[0], oracle.rms_norm(q[sl], wq, EPS), f"Q member {i}")
+        check_rotated_close(ring_k[i], ref_k[0], _ring_normed(k[None, sl], wk, offsets[i] % capacity, capacity, hw,
+                                                              frames[i]), f"K member {i}")
         assert torch.equal(ring_v[i], ref_v[0]), i
 
 
-def test_config1_fp32_first_chunk():
+@pytest.mark.parametrize("kernel", ["bulk", "rows"])
+def test_config1_fp32_first_chunk(kernel):
     """BASELINE config 1 in fp32: q,k [1, 4680, 12, 128], grid 3x30x52, offset 0 (no ring)."""
     H, D, gh, gw = 12, 128, 30, 52
     C, L = H * D, 3 * 30 * 52
@@ -245,7 +288,8 @@ def test_config1_fp32_first_chunk():
     dq, dk = q.to(DEV), k.to(DEV)
     q_out, k_out = torch.empty_like(dq), torch.empty_like(dk)
     qk_norm_rope_kv(heads=H, head_dim=D, seqs=[ops.flat_seq(0, L, gh, gw, 0)], cos=cos.to(DEV), sin=sin.to(DEV),
-                    q=dq, k=dk, q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=k_out)
+                    q=dq, k=dk, q_weight=wq.to(DEV), k_weight=wk.to(DEV), eps=EPS, q_out=q_out, k_out=k_out,
+                    kernel=kernel)
     torch.cuda.synchronize()
     ct, st = token_tables(cos, sin, split, 0, 3, gh, gw)
     for got, x, w in ((q_out.cpu(), q, wq), (k_out.cpu(), k, wk)):
@@ -291,14 +335,27 @@ def test_qkv_fused_buffer_strides():
     ref_k = torch.zeros(1, 60, C, dtype=torch.bfloat16)
     ref_v = torch.zeros_like(ref_k)
     ref_q = oracle.prep_ring(q, k, v, wq, wk, EPS, cos, sin, split, gh, gw, [7], ref_k, ref_v, [2])
-    check_bf16_close(q_out.cpu(), ref_q[0], "Q from QKV buffer")
-    check_bf16_close(ring_k.cpu(), ref_k[0], "K from QKV buffer")
+    check_rotated_close(q_out.cpu(), ref_q[0], oracle.rms_norm(q[0], wq, EPS), "Q from QKV buffer")
+    check_rotated_close(ring_k.cpu(), ref_k[0], _ring_normed(k, wk, 2, 3, 20, 2), "K from QKV buffer")
     assert torch.equal(ring_v.cpu(), ref_v[0])
 
 
 # ---------------------------------------------------------------------------------------
 # The drop-in processor and the ring layout against the reference's recorded prep
 # ---------------------------------------------------------------------------------------
+def _normed_heads(x, weight, eps, heads):
+    """The reference's RMSNorm output of projections [B, L, C] as [B, heads, L, D]."""
+    n = oracle.rms_norm(x, weight, eps)
+    return n.view(n.shape[0], n.shape[1], heads, -1).transpose(1, 2)
+
+
+def _normed_window(g, chunk):
+    """The reference's pre-RoPE K window of ``chunk`` ([1, heads, tokens, D])."""
+    parts = [_normed_heads(g["inputs"][p]["k"], g["norm_k_weight"], g["eps"], g["heads"])
+             for p in [*oracle.history_chunks(chunk), chunk]]
+    return torch.cat(parts, dim=2)
+
+
 class _Replay(torch.nn.Module):
     """Stands in for a projection: returns the recorded projection output."""
 
@@ -371,8 +428,9 @@ def test_drop_in_processor_matches_reference_prep(golden):
             if rec is None:
                 continue
             q_rot, k_rot, v_win = (t.cpu() for t in captured["sdpa"])
-            check_bf16_close(q_rot, rec["q_rot"], f"Q' chunk {chunk}")
-            check_bf16_close(k_rot, rec["k_window_rot"], f"K window' chunk {chunk}")
+            check_rotated_close(q_rot, rec["q_rot"], _normed_heads(inputs["q"], g["norm_q_weight"], g["eps"], heads),
+                                f"Q' chunk {chunk}")
+            check_rotated_close(k_rot, rec["k_window_rot"], _normed_window(g, chunk), f"K window' chunk {chunk}")
             assert torch.equal(v_win, rec["v_window"]), chunk
             check_bf16_close(cache.page[0].contiguous().cpu(), rec["page_k"], f"page K chunk {chunk}")
             torch.testing.assert_close(out.float().cpu(), rec["out"].float(), atol=3e-2, rtol=3e-2)
@@ -399,7 +457,8 @@ def test_ring_layout_matches_reference_window(golden):
         rec = records.get(chunk)
         if rec is None:
             continue
-        check_bf16_close(q_rot.view(1, -1, heads, D).transpose(1, 2).cpu(), rec["q_rot"], f"Q' chunk {chunk}")
+        check_rotated_close(q_rot.view(1, -1, heads, D).transpose(1, 2).cpu(), rec["q_rot"],
+                            _normed_heads(inputs["q"], g["norm_q_weight"], g["eps"], heads), f"Q' chunk {chunk}")
         kw, vw = cache.window(chunk)
         want_k = rec["k_window_rot"][0].transpose(0, 1).flatten(1)   # [tokens, C] reference order
         want_v = rec["v_window"][0].transpose(0, 1).flatten(1)
@@ -413,7 +472,8 @@ def test_ring_layout_matches_reference_window(golden):
             base = cache.sink_rows + slot * hw
             order.extend(range(base, base + hw))
         got_k, got_v = got_k[order], got_v[order]
-        check_bf16_close(got_k, want_k, f"ring window K chunk {chunk}")
+        normed = _normed_window(g, chunk)[0].transpose(0, 1).flatten(1)
+        check_rotated_close(got_k, want_k, normed, f"ring window K chunk {chunk}")
         assert torch.equal(got_v, want_v), chunk
 
 
@@ -425,7 +485,13 @@ def test_prepare_reference_layout_batch_members(golden):
     q_rot, k_pre = prepare_reference_layout(b["q"].to(DEV), b["k"].to(DEV), heads, g["norm_q_weight"].to(DEV),
                                             g["norm_k_weight"].to(DEV), g["eps"],
                                             tuple(t.to(DEV) for t in b["own"]))
-    check_bf16_close(q_rot.view(2, -1, heads, D).transpose(1, 2).cpu(), b["q_rot"], "batch Q'")
+    check_rotated_close(q_rot.view(2, -1, heads, D).transpose(1, 2).cpu(), b["q_rot"],
+                        _normed_heads(b["q"], g["norm_q_weight"], g["eps"], heads), "batch Q'")
     for m in range(2):
         check_bf16_close(k_pre[m:m + 1].view(1, -1, heads, D).transpose(1, 2).contiguous().cpu(), b["pages_k"][m],
                          f"batch page {m}")
+
+
+def test_no_bounded_wait_ran_out():
+    """After every kernel above, the bulk kernel's bounded mbarrier waits never expired."""
+    assert ops.device_timeouts(reset=True) == 0
