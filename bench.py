@@ -385,7 +385,7 @@ def run_ours(args):
     work = Workload(args.workload, rank, world, device, ring_frames=args.ring_frames,
                     heads_per_thread=args.heads_per_thread, kernel=args.kernel, stages=args.stages,
                     groups=args.groups, ctas_per_sm=args.ctas_per_sm, row_threads=args.row_threads,
-                    release=args.release, vstages=args.vstages)
+                    release=args.release, vstages=args.vstages, vdepth=args.vdepth)
     if args.cells:
         work.launches_per_step = args.cells
         work.tokens_per_step = work.tokens_per_launch * args.cells
@@ -542,6 +542,7 @@ def main(argv=None):
     parser.add_argument("--row-threads", type=int, default=0, help="bulk kernel: threads per row group")
     parser.add_argument("--release", type=int, default=0, help="bulk kernel: stage release mode (0 auto, 1, 2)")
     parser.add_argument("--vstages", type=int, default=0, help="bulk kernel: V stages per CTA (0 = auto)")
+    parser.add_argument("--vdepth", type=int, default=0, help="bulk kernel: V stores in flight (0 = auto)")
     parser.add_argument("--cells", type=int, default=0, help="launches per step override (profiling runs)")
     args = parser.parse_args(argv)
     if args.warmup < 3:

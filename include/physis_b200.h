@@ -118,11 +118,11 @@ typedef struct ps_qk_prep_args {
   int32_t groups;       /* PS_KERNEL_BULK: consumer row groups per CTA; 0 = automatic */
   int32_t ctas_per_sm;  /* PS_KERNEL_BULK: persistent CTAs per SM; 0 = 1 */
   int32_t row_threads;  /* PS_KERNEL_BULK: threads per row group (multiple of 32); 0 = automatic */
-  int32_t release;      /* PS_KERNEL_BULK: 0 = automatic, 1 = free a stage as soon as its stores have
-                           read it, 2 = keep one store group in flight per row group (free the
-                           previous stage after the next token's stores are issued) */
+  int32_t release;      /* PS_KERNEL_BULK: 0 = automatic; 1 + d (d = 0..7) = each row group keeps
+                           up to d tokens' stores in flight and frees a stage once its stores
+                           have read it */
   int32_t vstages;      /* PS_KERNEL_BULK: shared-memory V stages per CTA; 0 = automatic */
-  int32_t reserved1;    /* must be 0 */
+  int32_t vdepth;       /* PS_KERNEL_BULK: V stores kept in flight (1..7, below vstages); 0 = automatic */
 
   int64_t in_rows;      /* rows of q, k, v, q_out, k_pre (bounds of token_start + n_tokens) */
   const void* q;  int64_t q_stride;   /* [in_rows, C]; NULL: no Q role */

@@ -69,7 +69,7 @@ class PsQkPrepArgs(ctypes.Structure):
         ("row_threads", ctypes.c_int32),
         ("release", ctypes.c_int32),
         ("vstages", ctypes.c_int32),
-        ("reserved1", ctypes.c_int32),
+        ("vdepth", ctypes.c_int32),
         ("in_rows", ctypes.c_int64),
         ("q", ctypes.c_void_p), ("q_stride", ctypes.c_int64),
         ("k", ctypes.c_void_p), ("k_stride", ctypes.c_int64),

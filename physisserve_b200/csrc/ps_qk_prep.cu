@@ -102,8 +102,9 @@ struct KParams {
   int32_t row_bytes;    // C * element size
   int32_t stage_bytes;  // bytes of one stage (q | k | v rows)
   int32_t load_bytes;   // bytes the producer loads into a stage
-  int32_t defer;        // 1: free a stage only after the group's next stores are issued
+  int32_t defer;        // store groups a row group keeps in flight before freeing stages (0..7)
   int32_t vstages;      // shared-memory V stages per CTA
+  int32_t vdepth;       // V stores kept in flight by the V drain (1..min(vstages - 1, 7))
   int32_t vstage_bytes;
   int32_t off_abort, off_partials, off_meta, off_vmeta, off_stages, off_vstages;
   int32_t cum[PS_MAX_SEQS + 1];
@@ -140,8 +141,7 @@ __device__ __forceinline__ int find_seq(const KParams& p, int g) {
   return lo;
 }
 
-__device__ __forceinline__ Token decode(const KParams& p, int g) {
-  const int s = find_seq(p, g);
+__device__ __forceinline__ Token decode_in(const KParams& p, int s, int g) {
   const DevSeq& sq = p.seq[s];
   const int l = g - p.cum[s];
   const int f = static_cast<int>(div_by(static_cast<uint32_t>(l), sq.hw_magic));
@@ -161,6 +161,8 @@ __device__ __forceinline__ Token decode(const KParams& p, int g) {
   }
   return t;
 }
+
+__device__ __forceinline__ Token decode(const KParams& p, int g) { return decode_in(p, find_seq(p, g), g); }
 
 template <int P>
 struct Rot {
@@ -403,6 +405,20 @@ __device__ __forceinline__ void bulk_wait_read() {
 
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Waits until at most n (0..7) committed bulk groups still read shared memory.
+__device__ __forceinline__ void bulk_wait_read_upto(int n) {
+  switch (n) {
+    case 0: bulk_wait_read<0>(); break;
+    case 1: bulk_wait_read<1>(); break;
+    case 2: bulk_wait_read<2>(); break;
+    case 3: bulk_wait_read<3>(); break;
+    case 4: bulk_wait_read<4>(); break;
+    case 5: bulk_wait_read<5>(); break;
+    case 6: bulk_wait_read<6>(); break;
+    default: bulk_wait_read<7>(); break;
+  }
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void named_sync(int id, int threads) {
@@ -486,9 +502,11 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
       const T* kb = static_cast<const T*>(p.k);
       const T* vb = static_cast<const T*>(p.v);
       int issued = 0, vissued = 0;
+      int cursor = 0;  // sequence of the current token: tokens only move forward
       for (int i = 0; i < n_local; ++i) {
         const int g = static_cast<int>(blockIdx.x) + i * G;
-        const Token t = decode(p, g);
+        while (cursor + 1 < p.n_seqs && p.cum[cursor + 1] <= g) ++cursor;
+        const Token t = decode_in(p, cursor, g);
         if (flags & kHasV) {
           const int sv = i % SV;
           if (i >= SV && !mbar_wait(&vempty[sv], ((i / SV) & 1) ^ 1)) break;
@@ -519,19 +537,22 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
     // ---------------- V ring: store each row as soon as it lands ----------------
     if (threadIdx.x == 32 && (flags & kHasV)) {
       T* vout = static_cast<T*>(p.v_out);
-      int pending = -1;
+      // Up to `depth` stores stay in flight; a stage is freed once its store has read it.
+      const int depth = p.vdepth;
+      int released = 0;
+      int stored = 0;
       for (int i = 0; i < n_local; ++i) {
         const int sv = i % SV;
         if (!mbar_wait(&vfull[sv], (i / SV) & 1)) break;
         bulk_store(vout + vmeta[sv] * p.v_out_stride, v_stages + static_cast<size_t>(sv) * p.vstage_bytes,
                    p.row_bytes);
         bulk_commit();
-        bulk_wait_read<1>();
-        if (pending >= 0) mbar_arrive(&vempty[pending]);
-        pending = sv;
+        stored = i + 1;
+        bulk_wait_read_upto(depth);
+        for (; released < stored - depth; ++released) mbar_arrive(&vempty[released % SV]);
       }
       bulk_wait_read<0>();
-      if (pending >= 0) mbar_arrive(&vempty[pending]);
+      for (; released < stored; ++released) mbar_arrive(&vempty[released % SV]);
       bulk_wait_all();
     }
     return;
@@ -551,7 +572,9 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
   const int nvec = p.C / E;  // 16-byte vectors per row
   const T* wqb = static_cast<const T*>(p.wq);
   const T* wkb = static_cast<const T*>(p.wk);
-  int pending = -1;  // leader, deferred release: stage whose stores may still read smem
+  // Leader: up to p.defer of this group's store groups stay in flight; k-th token of
+  // the group is i = rg + k*groups, its stage i % S is freed once its stores read it.
+  int released = 0, committed = 0;
 
   for (int i = rg; i < n_local; i += p.rows) {
     const int s = i % S;
@@ -676,22 +699,16 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
       if (flags & kHasQ) bulk_store(static_cast<T*>(p.q_out) + t.row * p.q_out_stride, sq, p.row_bytes);
       if (flags & kKOut) bulk_store(static_cast<T*>(p.k_out) + t.kv_row * p.k_out_stride, sk, p.row_bytes);
       bulk_commit();
+      ++committed;
       // A stage is free once its stores have read it (the global writes complete
-      // asynchronously).  Deferred: this token's stores stay in flight while the group
-      // computes its next token, and the previous token's stage is freed instead.
-      if (p.defer) {
-        bulk_wait_read<1>();
-        if (pending >= 0) mbar_arrive(&empty[pending]);
-        pending = s;
-      } else {
-        bulk_wait_read<0>();
-        mbar_arrive(&empty[s]);
-      }
+      // asynchronously); the newest p.defer store groups may still be reading.
+      bulk_wait_read_upto(p.defer);
+      for (; released < committed - p.defer; ++released) mbar_arrive(&empty[(rg + released * p.rows) % S]);
     }
   }
   if (leader) {
     bulk_wait_read<0>();
-    if (pending >= 0) mbar_arrive(&empty[pending]);
+    for (; released < committed; ++released) mbar_arrive(&empty[(rg + released * p.rows) % S]);
     bulk_wait_all();
   }
 }
@@ -879,12 +896,15 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   const int qk_stage_bytes = (2 * row_bytes + 127) & ~127;
   const int v_stage_bytes = (row_bytes + 127) & ~127;
   const int nvec = static_cast<int>(C / E);
-  const bool bulk_shape =
-      (32 % vph) == 0 && 2048 + 4 * qk_stage_bytes + 2 * v_stage_bytes <= kBulkSmemBudget;
+  // The bulk pipeline wins from rows of ~4 KB up (B200: C=3072 bf16 85% vs 64% of HBM peak,
+  // C=5120 95% vs 60%); on narrower rows its per-token fixed costs dominate and the
+  // register-load kernel is faster (C=1536 bf16: 65% vs 47%).
+  const bool bulk_shape = (32 % vph) == 0 && row_bytes >= 4096 &&
+                          2048 + 4 * qk_stage_bytes + 2 * v_stage_bytes <= kBulkSmemBudget;
   int kernel = a->kernel;
   if (kernel == PS_KERNEL_AUTO) kernel = bulk_shape ? PS_KERNEL_BULK : PS_KERNEL_ROWS;
-  if (a->release < 0 || a->release > 2) return fail(PS_ERR_SHAPE, "release mode %d unknown", a->release);
-  if (a->reserved1 != 0) return fail(PS_ERR_SHAPE, "reserved1 must be 0");
+  if (a->release < 0 || a->release > 8) return fail(PS_ERR_SHAPE, "release mode %d unknown", a->release);
+  if (a->vdepth < 0 || a->vdepth > 7) return fail(PS_ERR_SHAPE, "vdepth %d outside 0..7", a->vdepth);
 
   k.q = a->q; k.k = a->k; k.v = a->v; k.wq = norm_q ? a->q_weight : nullptr; k.wk = norm_k ? a->k_weight : nullptr;
   k.cos = a->cos; k.sin = a->sin;
@@ -972,14 +992,22 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   const int head = header(stages, vstages, groups);
   const size_t layout = static_cast<size_t>(head) + static_cast<size_t>(stages) * qk_stage_bytes +
                         static_cast<size_t>(vstages) * v_stage_bytes;
-  const bool defer = a->release == 2 || (a->release == 0 && stages >= 2 * groups + 2);
-  if (stages < (defer ? 2 * groups + 1 : groups + 1) || layout > static_cast<size_t>(kBulkSmemBudget))
+  // Store groups each row group keeps in flight (release mode 1 + depth, 0 = automatic:
+  // as deep as the stages allow while one stage per group stays free for loading).
+  int depth = a->release > 0 ? a->release - 1 : (stages - 2 * groups) / groups;
+  if (depth < 0) depth = 0;
+  if (depth > 7) depth = 7;
+  if (stages < groups * (depth + 1) + 1 || layout > static_cast<size_t>(kBulkSmemBudget))
     return fail(PS_ERR_UNSUPPORTED, "%d stages of %d bytes for %d row groups do not fit shared memory", stages,
                 qk_stage_bytes, groups);
-  k.defer = defer ? 1 : 0;
+  k.defer = depth;
   k.rows = groups;
   k.stages = stages;
   k.vstages = vstages;  // 0 without a V role
+  int vdepth = a->vdepth > 0 ? a->vdepth : 2;  // two V stores in flight measured best (C = 3072, 5120)
+  if (vdepth > vstages - 1) vdepth = vstages - 1;
+  if (vdepth < 1) vdepth = 1;
+  k.vdepth = vdepth;
   k.row_bytes = row_bytes;
   k.stage_bytes = qk_stage_bytes;
   k.vstage_bytes = v_stage_bytes;

@@ -173,6 +173,7 @@ def qk_norm_rope_kv(
     row_threads: int = 0,
     release: int = 0,
     vstages: int = 0,
+    vdepth: int = 0,
 ) -> None:
     """One fused launch (per ``PS_MAX_SEQS`` sequences) of ``ps_qk_norm_rope_kv``.
 
@@ -183,7 +184,7 @@ def qk_norm_rope_kv(
     [rows, D] or the reference's [B, L, 1, D] tables, read at ``table_row + l``).
     ``kernel`` is "auto", "bulk" (persistent cp.async.bulk pipeline) or "rows"; the tiling
     knobs (``heads_per_thread`` for rows; ``row_threads``, ``stages``, ``groups``,
-    ``ctas_per_sm``, ``release``, ``vstages`` for bulk) default to the library's choice.
+    ``ctas_per_sm``, ``release``, ``vstages``, ``vdepth`` for bulk) default to the library's choice.
     """
     C = heads * head_dim
     ref = next(t for t in (q, k, v) if t is not None)
@@ -231,7 +232,7 @@ def qk_norm_rope_kv(
             dtype=dtype, heads=heads, head_dim=head_dim, table_mode=mode,
             t_dim=split[0], h_dim=split[1], w_dim=split[2], n_seqs=len(part), eps=float(eps),
             heads_per_thread=heads_per_thread, kernel=_KERNELS[kernel], stages=stages, groups=groups,
-            ctas_per_sm=ctas_per_sm, row_threads=row_threads, release=release, vstages=vstages, in_rows=in_rows,
+            ctas_per_sm=ctas_per_sm, row_threads=row_threads, release=release, vstages=vstages, vdepth=vdepth, in_rows=in_rows,
             q=qp, q_stride=qs, k=kp, k_stride=ks, v=vp, v_stride=vs,
             q_weight=None if q_weight is None else q_weight.data_ptr(),
             k_weight=None if k_weight is None else k_weight.data_ptr(),

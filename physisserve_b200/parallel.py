@@ -1,0 +1,121 @@
+"""Multi-GPU placement of the attention-prep path: stream sharding and the 2-stage handoff.
+
+The prep kernels have no collective: every stream (its chunk, its KV ring) is independent,
+so streams are sharded over GPUs (``shard_streams``), the way PhysisServe's pool placement
+puts whole streams on disjoint GPU sets (physisserve/engine/strategies/placement.py:186-263,
+MappedLayout 237-263).  The pipelined configuration splits the DiT's blocks into stages
+(StageEqual, engine/strategies/stage_equal.py:21-57): a stage runs its blocks for a chunk's
+denoising step, then hands the hidden state [tokens, C] to the next stage with a
+point-to-point send/recv, as the reference's transport does with batch_isend_irecv
+(engine/transport.py:116-150).  Only the hidden state crosses GPUs; each stage keeps the KV
+history of its own blocks, so no KV ever moves (model_runner.py:44-69).
+"""
+from __future__ import annotations
+
+import datetime
+from dataclasses import dataclass
+from typing import Callable, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def shard_streams(n_streams: int, rank: int, world: int) -> list[int]:
+    """Streams owned by ``rank``: stream i runs on GPU i mod world (disjoint and complete)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    return list(range(rank, n_streams, world))
+
+
+def stage_blocks(stage: int, stages: int, num_blocks: int) -> range:
+    """Contiguous equal split of the blocks over stages (StageEqual's layout)."""
+    if not 0 <= stage < stages or stages > num_blocks:
+        raise ValueError(f"stage {stage} of {stages} for {num_blocks} blocks")
+    base, extra = divmod(num_blocks, stages)
+    start = stage * base + min(stage, extra)
+    return range(start, start + base + (1 if stage < extra else 0))
+
+
+@dataclass(frozen=True)
+class PipelineLayout:
+    """Ranks grouped into pipelines of ``stages`` consecutive ranks; streams sharded over pipelines."""
+
+    world: int
+    stages: int
+
+    def __post_init__(self):
+        if self.stages < 1 or self.world % self.stages:
+            raise ValueError(f"{self.world} ranks do not split into pipelines of {self.stages} stages")
+
+    @property
+    def pipelines(self) -> int:
+        return self.world // self.stages
+
+    def stage_of(self, rank: int) -> int:
+        return rank % self.stages
+
+    def pipeline_of(self, rank: int) -> int:
+        return rank // self.stages
+
+    def peer(self, rank: int, offset: int) -> int:
+        """The rank ``offset`` stages after ``rank`` in its pipeline (wrapping around)."""
+        p = self.pipeline_of(rank)
+        return p * self.stages + (self.stage_of(rank) + offset) % self.stages
+
+    def streams(self, n_streams: int, rank: int) -> list[int]:
+        return shard_streams(n_streams, self.pipeline_of(rank), self.pipelines)
+
+
+def pipeline_tick(layout: PipelineLayout, rank: int, hidden: torch.Tensor,
+                  run_blocks: Callable[[torch.Tensor], torch.Tensor], group=None) -> torch.Tensor:
+    """One tick of a ring pipeline with one micro-batch per stage.
+
+    Every stage runs its blocks on the micro-batch it holds, then all stages exchange in one
+    grouped send/recv: the result goes to the next stage and the previous stage's result
+    arrives in ``hidden`` (the last stage feeds stage 0, which starts that micro-batch's next
+    denoising step).  Grouping the send with the receive makes the exchange deadlock-free for
+    any number of stages.  Returns ``hidden`` holding the received micro-batch.
+    """
+    out = run_blocks(hidden)
+    if layout.stages == 1:
+        hidden.copy_(out)
+        return hidden
+    _exchange(send=(out, layout.peer(rank, 1)), recv=(hidden, layout.peer(rank, -1)), group=group)
+    return hidden
+
+
+def _exchange(send=None, recv=None, group=None):
+    ops = []
+    if send is not None:
+        ops.append(dist.P2POp(dist.isend, send[0].contiguous(), send[1], group=group))
+    if recv is not None:
+        ops.append(dist.P2POp(dist.irecv, recv[0], recv[1], group=group))
+    for work in dist.batch_isend_irecv(ops):
+        work.wait()
+
+
+def init_process_group(backend: str, timeout_s: float = 60.0, device_id=None):
+    """Process group from the torchrun environment with a short timeout, so a rank that
+    fails makes its peers' next collective end with an error instead of waiting."""
+    kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if device_id is not None:
+        kwargs["device_id"] = device_id
+    dist.init_process_group(backend, **kwargs)
+    return dist.get_rank(), dist.get_world_size()
+
+
+def max_over_ranks(value: float, device=None) -> float:
+    """Maximum of a per-rank value (device timings are reported as the max over ranks)."""
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(values: Sequence[float], device=None) -> list[float]:
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return [float(v) for v in values]
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(v) for v in t.tolist()]

@@ -117,8 +117,8 @@ def test_validate_accepts_config2(lib):
     (dict(kernel=_lib.KERNEL_BULK, row_threads=48), _lib.ERR_UNSUPPORTED, "multiple of 32"),
     (dict(kernel=_lib.KERNEL_BULK, groups=4, stages=3), _lib.ERR_UNSUPPORTED, "do not fit"),
     (dict(kernel=9), _lib.ERR_SHAPE, "kernel 9 unknown"),
-    (dict(release=3), _lib.ERR_SHAPE, "release mode 3 unknown"),
-    (dict(reserved1=1), _lib.ERR_SHAPE, "reserved1"),
+    (dict(release=9), _lib.ERR_SHAPE, "release mode 9 unknown"),
+    (dict(vdepth=8), _lib.ERR_SHAPE, "vdepth 8"),
     (dict(kernel=_lib.KERNEL_BULK, release=2, groups=3, stages=6), _lib.ERR_UNSUPPORTED, "do not fit"),
 ])
 def test_validate_rejects(lib, over, status, text):

@@ -145,7 +145,7 @@ def test_fused_small_bit_exact_rope_and_slots(kernel, tile):
 
 @pytest.mark.parametrize("stages,groups,ctas,release,vstages", [
     (3, 1, 1, 1, 2), (4, 2, 1, 1, 3), (9, 4, 2, 2, 0), (0, 0, 1, 0, 0), (5, 3, 1, 1, 2), (3, 1, 1, 2, 5),
-    (7, 3, 1, 2, 16)])
+    (7, 3, 1, 2, 16), (13, 3, 1, 4, 9), (17, 2, 1, 8, 8), (0, 6, 1, 0, 0)])
 def test_bulk_pipeline_shapes(stages, groups, ctas, release, vstages):
     """The bulk kernel over few / many stages and row groups, with more tokens than CTAs so
     every stage is reused many times (exercises the full/empty mbarrier phases)."""
