@@ -484,6 +484,99 @@ def run_ours(args):
     return 0
 
 
+def run_pipeline(args):
+    """BASELINE config 5, pipelined: 2-stage pipelines of 15 blocks per GPU over NCCL send/recv.
+
+    Ranks form pipelines of two consecutive ranks; the 64 streams are sharded over pipelines
+    and split into two micro-batches per pipeline.  Each tick every stage runs its 15 blocks
+    (one fused prep launch per block over the micro-batch's streams, Q taken from the hidden
+    state it holds) and then hands the hidden state [tokens, 1536] bf16 to the other stage with
+    one grouped send/recv (physisserve_b200.parallel.pipeline_tick).  4 denoising steps x 2
+    stages = 8 ticks move a micro-batch through the 30 blocks x 4 steps of a chunk.
+    """
+    import torch.distributed as dist
+
+    from physisserve_b200.ops import Seq, qk_norm_rope_kv
+    from physisserve_b200.parallel import PipelineLayout, pipeline_tick, stage_blocks
+    from physisserve_b200.wan import wan_rope_tables
+
+    rank, world, local = init_dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world < 2 or world % 2:
+        raise SystemExit("--pipeline needs an even number of GPUs (2-stage pipelines)")
+    layout = PipelineLayout(world=world, stages=2)
+    spec = WORKLOADS["cfg5"]
+    streams = layout.streams(spec["streams"], rank)
+    micro = streams[layout.stage_of(rank)::2]  # the micro-batch this stage starts with
+    heads, D = spec["heads"], spec["head_dim"]
+    C, hw = heads * D, spec["grid"][1] * spec["grid"][2]
+    T = len(micro) * hw
+    blocks = stage_blocks(layout.stage_of(rank), 2, 30)
+    g = torch.Generator().manual_seed(77 + rank)
+    hidden = torch.randn(T, C, generator=g).bfloat16().to(device)
+    k = torch.randn(T, C, generator=g).bfloat16().to(device)
+    v = torch.randn(T, C, generator=g).bfloat16().to(device)
+    wq = [(torch.rand(C, generator=g) + 0.5).bfloat16().to(device) for _ in blocks]
+    wk = [(torch.rand(C, generator=g) + 0.5).bfloat16().to(device) for _ in blocks]
+    cos, sin = wan_rope_tables(D, 4096, device=device)
+    capacity = spec["capacity"]
+    rows = capacity * hw
+    ring_k = torch.zeros(len(micro) * rows, C, device=device, dtype=torch.bfloat16)
+    ring_v = torch.zeros_like(ring_k)
+    out = torch.empty(T, C, device=device, dtype=torch.bfloat16)
+    rng = random.Random(5 + rank)
+    offsets = [rng.randint(*spec["offsets"]) for _ in micro]
+    seqs = [Seq(i * hw, hw, spec["grid"][1], spec["grid"][2], frame_offset=o, ring_row=i * rows,
+                ring_frames=capacity, ring_slot0=o % capacity) for i, o in enumerate(offsets)]
+    launches = [0]
+
+    def run_blocks(h):
+        src = h
+        for b in range(len(blocks)):
+            qk_norm_rope_kv(heads=heads, head_dim=D, seqs=seqs, cos=cos, sin=sin, q=src, k=k, v=v, q_weight=wq[b],
+                            k_weight=wk[b], eps=1e-6, q_out=out, k_out=ring_k, v_out=ring_v)
+            launches[0] += 1
+            src = out
+        return out
+
+    for _ in range(args.warmup):
+        hidden = pipeline_tick(layout, rank, hidden, run_blocks)
+    torch.cuda.synchronize()
+    dist.barrier()
+    stream = torch.cuda.current_stream(device)
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    launches[0] = 0
+    torch.cuda.synchronize()
+    sampler.start()
+    begin.record(stream)
+    for _ in range(args.steps):
+        hidden = pipeline_tick(layout, rank, hidden, run_blocks)
+    finish.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    dist.barrier()
+    ms = max_over_ranks(begin.elapsed_time(finish), world, device)
+    tokens = sum(gather_objects(T * len(blocks) * args.steps, world))
+    all_clocks = gather_objects(clocks, world)
+    if rank == 0:
+        line = {
+            "metric": "rotated_qk_tokens_per_s", "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": "cfg5-pipelined", "desc": "64 streams, 2-stage pipelines x 15 blocks, NCCL "
+                       "send/recv of the [tokens, 1536] bf16 hidden state each tick",
+                       "pipelines": layout.pipelines, "tokens_per_microbatch": T,
+                       "handoff_bytes_per_tick": T * C * 2, "step": "one pipeline tick"},
+            "clocks": {"per_rank": all_clocks, **all_clocks[0]},
+            "gpu_launches": launches[0], "e2e": None,
+        }
+        print(json.dumps(line))
+    dist.destroy_process_group()
+    return 0
+
+
 def run_e2e(args, work, world, device, stream):
     """The public API end to end: H2D of q, k, v from pinned host memory, the fused prep
     through physisserve_b200.ops.qk_norm_rope_kv, D2H of the rotated Q (every step)."""
@@ -544,11 +637,15 @@ def main(argv=None):
     parser.add_argument("--vstages", type=int, default=0, help="bulk kernel: V stages per CTA (0 = auto)")
     parser.add_argument("--vdepth", type=int, default=0, help="bulk kernel: V stores in flight (0 = auto)")
     parser.add_argument("--cells", type=int, default=0, help="launches per step override (profiling runs)")
+    parser.add_argument("--pipeline", action="store_true",
+                        help="BASELINE config 5 pipelined: 2-stage pipelines (15 blocks per GPU) over NCCL")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
     if args.impl == "reference":
         return run_reference(args)
+    if args.pipeline:
+        return run_pipeline(args)
     return run_ours(args)
 
 

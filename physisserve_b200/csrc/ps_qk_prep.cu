@@ -734,11 +734,15 @@ static int pow2_segment(int tpr) {
 
 static bool supported_v(int v) { return v == 1 || v == 2 || v == 3 || v == 4 || v == 5 || v == 6 || v == 8; }
 
-// Chooses heads-per-thread V: prefer V >= 2 with a warp-multiple row group of
-// at most 256 threads (several loads in flight per thread, few registers),
-// then any warp-multiple group, then (rows_kernel only) any group that fits.
+// Chooses heads-per-thread V for rows_kernel.  Measured on B200: row groups of 64-128
+// threads with at most 3 heads per thread (few registers, many row groups per SM) are
+// fastest -- C=1536 bf16: V=3 (64 threads) 87% of HBM peak vs V=2 (96 threads) 65%;
+// C=3072: V=3 (128 threads) 84% vs V=6 (64 threads) 68%.  Otherwise any warp-multiple
+// group, then (rows_kernel only) any group that fits.
 static int choose_v(int heads, int vph, int max_threads, bool warp_multiple) {
-  const int order[] = {2, 3, 4, 5, 6, 8, 1};
+  for (int v : {3, 2, 1})
+    if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= 128) return v;
+  const int order[] = {4, 5, 6, 8, 3, 2, 1};
   for (int v : order)
     if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= 256) return v;
   for (int v : order)
@@ -962,9 +966,11 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   k.hstep = 0;
   k.seg = 32;
   k.nseg = tpr / 32;
-  // Shared memory: V stages take about a quarter of the budget (they are short-lived),
-  // q|k stages the rest.
-  int vstages = has_v ? (a->vstages > 0 ? a->vstages : kBulkSmemBudget / 4 / v_stage_bytes) : 0;
+  // Shared memory: four V stages (they are short-lived), q|k stages the rest.  With the V
+  // drain keeping vdepth = vstages - 2 stores in flight, exactly two V stages stay free for
+  // the producer: one starves the V loads, three or more let V run ahead of Q/K (B200, C=5120:
+  // 124 us vs 154 us and 128-133 us per 767 MB launch).
+  int vstages = has_v ? (a->vstages > 0 ? a->vstages : 4) : 0;
   if (has_v && vstages < 2) vstages = 2;
   if (vstages > 32) vstages = 32;
   auto header = [&](int S, int SV, int groups) {
@@ -1004,7 +1010,7 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   k.rows = groups;
   k.stages = stages;
   k.vstages = vstages;  // 0 without a V role
-  int vdepth = a->vdepth > 0 ? a->vdepth : 2;  // two V stores in flight measured best (C = 3072, 5120)
+  int vdepth = a->vdepth > 0 ? a->vdepth : vstages - 2;
   if (vdepth > vstages - 1) vdepth = vstages - 1;
   if (vdepth < 1) vdepth = 1;
   k.vdepth = vdepth;
