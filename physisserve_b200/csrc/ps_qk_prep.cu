@@ -162,60 +162,6 @@ __device__ __forceinline__ Token decode_in(const KParams& p, int s, int g) {
   return t;
 }
 
-__device__ __forceinline__ Token decode(const KParams& p, int g) { return decode_in(p, find_seq(p, g), g); }
-
-template <int P>
-struct Rot {
-  float ce[P], co[P], se[P], so[P];
-};
-
-template <int P>
-__device__ __forceinline__ void load_rot(const KParams& p, const Token& t, int dvec, Rot<P>& r) {
-#pragma unroll
-  for (int j = 0; j < P; ++j) {
-    const int pair = dvec * P + j;
-    const int64_t trow = pair < p.tp ? t.trow_t : (pair < p.thp ? t.trow_h : t.trow_w);
-    const float2 c = __ldg(reinterpret_cast<const float2*>(p.cos + trow * p.head_dim + 2 * pair));
-    const float2 s = __ldg(reinterpret_cast<const float2*>(p.sin + trow * p.head_dim + 2 * pair));
-    r.ce[j] = c.x;
-    r.co[j] = c.y;
-    r.se[j] = s.x;
-    r.so[j] = s.y;
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ float sum_squares(const uint4& v) {
-  constexpr int E = Vec16<T>::kElems;
-  float x[E];
-  Vec16<T>::unpack(v, x);
-  float acc = 0.f;
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc = fmaf(x[e], x[e], acc);
-  return acc;
-}
-
-// y = round((x * rstd) * w) -- torch.nn.RMSNorm's single rounding to the element type.
-template <typename T>
-__device__ __forceinline__ void normalise(float* x, const uint4& wv, float rstd) {
-  constexpr int E = Vec16<T>::kElems;
-  float w[E];
-  Vec16<T>::unpack(wv, w);
-#pragma unroll
-  for (int e = 0; e < E; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], rstd), w[e]);
-#pragma unroll
-  for (int e = 0; e < E; e += 2) Vec16<T>::round_pair(x[e], x[e + 1]);
-}
-
-template <typename T, int P>
-__device__ __forceinline__ uint4 rotate(const float* x, const Rot<P>& r) {
-  float y[2 * P];
-#pragma unroll
-  for (int j = 0; j < P; ++j)
-    rotate_pair(x[2 * j], x[2 * j + 1], r.ce[j], r.co[j], r.se[j], r.so[j], y[2 * j], y[2 * j + 1]);
-  return Vec16<T>::pack(y);
-}
-
 __device__ __forceinline__ float rstd_of(float ssq, float c, float eps) {
   // 1 / sqrt(mean(x^2) + eps), each step IEEE-rounded (torch's CPU rsqrt is 1/sqrt).
   return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssq, c), eps)));
@@ -247,70 +193,119 @@ __device__ __forceinline__ void reduce_row(const KParams& p, float2* partials, i
 // ------------------------------------------------------------------------------------
 // rows_kernel: one row group per token, register loads
 // ------------------------------------------------------------------------------------
-template <typename T, int V>
+// Flag sets with specialised kernels (the remaining combinations run the generic
+// instantiation, FLAGS = 0, which reads the flags at run time).
+constexpr int kModeRing = kHasQ | kHasK | kHasV | kNormQ | kNormK | kKOut;  // ring layout prep
+constexpr int kModeRef = kHasQ | kHasK | kNormQ | kNormK | kKPre;           // reference-layout prep
+constexpr int kModeSink = kHasK | kKOut;                                    // sink re-rotation
+
+// The rotation of one pair (e, o) with cos pair (cos[2i], cos[2i+1]) and sin pair
+// (sin[2i], sin[2i+1]): two packed products and two scalar adds, the three roundings of
+// _rope per output (wan.py:61-62).
+__device__ __forceinline__ void rotate_f2(f32x2 x, f32x2 c, f32x2 sn, float& lo, float& hi) {
+  float m1e, m1o, m2e, m2o;
+  f2_split(f2_mul(x, c), m1e, m1o);   // (e*cos[2i], o*cos[2i+1])
+  f2_split(f2_mul(x, sn), m2e, m2o);  // (e*sin[2i], o*sin[2i+1])
+  lo = __fsub_rn(m1e, m2o);
+  hi = __fadd_rn(m1o, m2e);
+}
+
+template <typename T, int V, int FLAGS>
 __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant__ KParams p) {
-  using VT = Vec16<T>;
-  constexpr int E = VT::kElems;
-  constexpr int P = E / 2;
+  using PT = Pairs16<T>;
+  constexpr int E = Vec16<T>::kElems;
+  constexpr int P = PT::kPairs;
   extern __shared__ float2 partials[];  // [rows][nseg]
+  const int flags = FLAGS ? FLAGS : p.flags;
 
   const int rg = threadIdx.x / p.tpr;
   const int lt = threadIdx.x - rg * p.tpr;
   const int dvec = lt % p.vph;
   const int head0 = lt / p.vph;
-  const int g = blockIdx.x * p.rows + rg;
-  const bool active = g < p.total;
-  const int flags = p.flags;
-  const Token t = decode(p, active ? g : 0);
+  const int g0 = blockIdx.x * p.rows + rg;
+  const bool active = g0 < p.total;
+  const int g = active ? g0 : 0;
+  // The row first, so the loads are issued before the rest of the decode.
+  const int sidx = find_seq(p, g);
+  const int64_t row = p.seq[sidx].row0 + (g - p.cum[sidx]);
 
   int elem_off[V];
 #pragma unroll
   for (int i = 0; i < V; ++i) elem_off[i] = (head0 + i * p.hstep) * p.head_dim + dvec * E;
 
-  const T* qrow = static_cast<const T*>(p.q) + t.row * p.q_stride;
-  const T* krow = static_cast<const T*>(p.k) + t.row * p.k_stride;
-  const T* vrow = static_cast<const T*>(p.v) + t.row * p.v_stride;
-
-  uint4 qv[V], kv[V];
+  uint4 qv[V], kv[V], vv[V];
   if (active) {
+    const T* qrow = static_cast<const T*>(p.q) + row * p.q_stride;
+    const T* krow = static_cast<const T*>(p.k) + row * p.k_stride;
+    const T* vrow = static_cast<const T*>(p.v) + row * p.v_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       if (flags & kHasQ) qv[i] = ld_stream(qrow + elem_off[i]);
       if (flags & kHasK) kv[i] = ld_stream(krow + elem_off[i]);
+      if (flags & kHasV) vv[i] = ld_stream(vrow + elem_off[i]);
+    }
+  }
+  const Token t = decode_in(p, sidx, g);
+  f32x2 cc[P], ss[P];
+  if (active && (flags & (kHasQ | kHasK))) {
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int pair = dvec * P + j;
+      const int64_t trow = pair < p.tp ? t.trow_t : (pair < p.thp ? t.trow_h : t.trow_w);
+      cc[j] = __ldg(reinterpret_cast<const unsigned long long*>(p.cos + trow * p.head_dim + 2 * pair));
+      ss[j] = __ldg(reinterpret_cast<const unsigned long long*>(p.sin + trow * p.head_dim + 2 * pair));
     }
   }
   if (active && (flags & kHasV)) {
-    uint4 vv[V];
-#pragma unroll
-    for (int i = 0; i < V; ++i) vv[i] = ld_stream(vrow + elem_off[i]);
     T* vout = static_cast<T*>(p.v_out) + t.kv_row * p.v_out_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) st_vec(vout + elem_off[i], vv[i]);
   }
-  Rot<P> r;
-  if (active && (flags & (kHasQ | kHasK))) load_rot<P>(p, t, dvec, r);
 
   float ssq_q = 0.f, ssq_k = 0.f;
-  if (active) {
+  if (active && (flags & (kNormQ | kNormK))) {
+    f32x2 aq = 0, ak = 0;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      if (flags & kNormQ) ssq_q += sum_squares<T>(qv[i]);
-      if (flags & kNormK) ssq_k += sum_squares<T>(kv[i]);
+      f32x2 x[P];
+      if (flags & kNormQ) {
+        PT::unpack(qv[i], x);
+#pragma unroll
+        for (int j = 0; j < P; ++j) aq = f2_fma(x[j], x[j], aq);
+      }
+      if (flags & kNormK) {
+        PT::unpack(kv[i], x);
+#pragma unroll
+        for (int j = 0; j < P; ++j) ak = f2_fma(x[j], x[j], ak);
+      }
     }
+    float a, b;
+    f2_split(aq, a, b);
+    ssq_q = a + b;
+    f2_split(ak, a, b);
+    ssq_k = a + b;
   }
   if (flags & (kNormQ | kNormK)) reduce_row(p, partials + rg * p.nseg, lt, ssq_q, ssq_k, [] { __syncthreads(); });
   if (!active) return;
-  const float rstd_q = rstd_of(ssq_q, p.c_f, p.eps);
-  const float rstd_k = rstd_of(ssq_k, p.c_f, p.eps);
+  const float rq = rstd_of(ssq_q, p.c_f, p.eps);
+  const float rk = rstd_of(ssq_k, p.c_f, p.eps);
+  const f32x2 rq2 = f2_make(rq, rq), rk2 = f2_make(rk, rk);
 
   if (flags & kHasQ) {
     T* qout = static_cast<T*>(p.q_out) + t.row * p.q_out_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float x[E];
-      VT::unpack(qv[i], x);
-      if (flags & kNormQ) normalise<T>(x, ld_keep(static_cast<const T*>(p.wq) + elem_off[i]), rstd_q);
-      st_vec(qout + elem_off[i], rotate<T, P>(x, r));
+      f32x2 x[P], w[P];
+      PT::unpack(qv[i], x);
+      if (flags & kNormQ) {
+        PT::unpack(ld_keep(static_cast<const T*>(p.wq) + elem_off[i]), w);
+#pragma unroll
+        for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rq2), w[j]));
+      }
+      float lo[P], hi[P];
+#pragma unroll
+      for (int j = 0; j < P; ++j) rotate_f2(x[j], cc[j], ss[j], lo[j], hi[j]);
+      st_vec(qout + elem_off[i], PT::pack(lo, hi));
     }
   }
   if (flags & kHasK) {
@@ -318,15 +313,24 @@ __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant
     T* kpre = static_cast<T*>(p.k_pre) + t.row * p.k_pre_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      float x[E];
-      VT::unpack(kv[i], x);
+      f32x2 x[P], w[P];
+      PT::unpack(kv[i], x);
       if (flags & kNormK) {
-        normalise<T>(x, ld_keep(static_cast<const T*>(p.wk) + elem_off[i]), rstd_k);
-        if (flags & kKPre) st_vec(kpre + elem_off[i], VT::pack(x));
-      } else if (flags & kKPre) {
-        st_vec(kpre + elem_off[i], kv[i]);
+        PT::unpack(ld_keep(static_cast<const T*>(p.wk) + elem_off[i]), w);
+#pragma unroll
+        for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rk2), w[j]));
       }
-      if (flags & kKOut) st_vec(kout + elem_off[i], rotate<T, P>(x, r));
+      float lo[P], hi[P];
+      if (flags & kKPre) {
+#pragma unroll
+        for (int j = 0; j < P; ++j) f2_split(x[j], lo[j], hi[j]);
+        st_vec(kpre + elem_off[i], (flags & kNormK) ? PT::pack(lo, hi) : kv[i]);
+      }
+      if (flags & kKOut) {
+#pragma unroll
+        for (int j = 0; j < P; ++j) rotate_f2(x[j], cc[j], ss[j], lo[j], hi[j]);
+        st_vec(kout + elem_off[i], PT::pack(lo, hi));
+      }
     }
   }
 }
@@ -433,11 +437,6 @@ struct StageMeta {
   int64_t trow_t, trow_h, trow_w;
 };
 
-// Flag sets with a specialised bulk_kernel (the remaining combinations run the
-// generic instantiation, FLAGS = 0, which reads the flags at run time).
-constexpr int kModeRing = kHasQ | kHasK | kHasV | kNormQ | kNormK | kKOut;  // ring layout prep
-constexpr int kModeRef = kHasQ | kHasK | kNormQ | kNormK | kKPre;           // reference-layout prep
-constexpr int kModeSink = kHasK | kKOut;                                    // sink re-rotation
 
 // bulk_kernel: warp 0 lane 0 is the producer, warp 1 lane 0 drains the V ring,
 // warps 2.. are the consumer row groups.
@@ -655,13 +654,7 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
         }
         float lo[P], hi[P];
 #pragma unroll
-        for (int j = 0; j < P; ++j) {
-          float m1e, m1o, m2e, m2o;
-          f2_split(f2_mul(x[j], cc[j]), m1e, m1o);  // (e*ce, o*co)
-          f2_split(f2_mul(x[j], ss[j]), m2e, m2o);  // (e*se, o*so)
-          lo[j] = __fsub_rn(m1e, m2o);              // e*cos[2i] - o*sin[2i+1]
-          hi[j] = __fadd_rn(m1o, m2e);              // o*cos[2i+1] + e*sin[2i]
-        }
+        for (int j = 0; j < P; ++j) rotate_f2(x[j], cc[j], ss[j], lo[j], hi[j]);
         *reinterpret_cast<uint4*>(sq + off) = PT::pack(lo, hi);
       }
       if (flags & kHasK) {
@@ -682,13 +675,7 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
         if (flags & kKOut) {
           float lo[P], hi[P];
 #pragma unroll
-          for (int j = 0; j < P; ++j) {
-            float m1e, m1o, m2e, m2o;
-            f2_split(f2_mul(x[j], cc[j]), m1e, m1o);
-            f2_split(f2_mul(x[j], ss[j]), m2e, m2o);
-            lo[j] = __fsub_rn(m1e, m2o);
-            hi[j] = __fadd_rn(m1o, m2e);
-          }
+          for (int j = 0; j < P; ++j) rotate_f2(x[j], cc[j], ss[j], lo[j], hi[j]);
           *reinterpret_cast<uint4*>(sk + off) = PT::pack(lo, hi);
         }
       }
@@ -734,15 +721,14 @@ static int pow2_segment(int tpr) {
 
 static bool supported_v(int v) { return v == 1 || v == 2 || v == 3 || v == 4 || v == 5 || v == 6 || v == 8; }
 
-// Chooses heads-per-thread V for rows_kernel.  Measured on B200: row groups of 64-128
-// threads with at most 3 heads per thread (few registers, many row groups per SM) are
-// fastest -- C=1536 bf16: V=3 (64 threads) 87% of HBM peak vs V=2 (96 threads) 65%;
-// C=3072: V=3 (128 threads) 84% vs V=6 (64 threads) 68%.  Otherwise any warp-multiple
-// group, then (rows_kernel only) any group that fits.
+// Chooses heads-per-thread V for rows_kernel: the most heads per thread (up to 6, the
+// largest count that fits the register budget without spilling) that keeps the row group
+// a whole number of warps.  More heads per thread means fewer threads per token, so the
+// per-token work -- sequence lookup, position decode, row reduction, rstd -- is shared by
+// fewer threads.  Measured on B200 (percent of the HBM copy peak): C=1536 bf16 V=6 (32
+// threads) 98%, V=3 (64) 89%, V=2 (96) 84%; C=3072 V=6 (64) 93%, V=3 (128) 87%.
 static int choose_v(int heads, int vph, int max_threads, bool warp_multiple) {
-  for (int v : {3, 2, 1})
-    if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= 128) return v;
-  const int order[] = {4, 5, 6, 8, 3, 2, 1};
+  const int order[] = {6, 5, 4, 3, 2, 1, 8};
   for (int v : order)
     if (heads % v == 0 && (vph * (heads / v)) % 32 == 0 && vph * (heads / v) <= 256) return v;
   for (int v : order)
@@ -900,10 +886,10 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   const int qk_stage_bytes = (2 * row_bytes + 127) & ~127;
   const int v_stage_bytes = (row_bytes + 127) & ~127;
   const int nvec = static_cast<int>(C / E);
-  // The bulk pipeline wins from rows of ~4 KB up (B200: C=3072 bf16 85% vs 64% of HBM peak,
-  // C=5120 95% vs 60%); on narrower rows its per-token fixed costs dominate and the
-  // register-load kernel is faster (C=1536 bf16: 65% vs 47%).
-  const bool bulk_shape = (32 % vph) == 0 && row_bytes >= 4096 &&
+  // The bulk pipeline is the faster kernel for rows of 8 KB and more (B200, C=5120 bf16: 95%
+  // vs 91% of the HBM copy peak); on narrower rows the register-load kernel wins (C=3072:
+  // 93% vs 81%, C=1536: 98% vs 47%).
+  const bool bulk_shape = (32 % vph) == 0 && row_bytes >= 8192 &&
                           2048 + 4 * qk_stage_bytes + 2 * v_stage_bytes <= kBulkSmemBudget;
   int kernel = a->kernel;
   if (kernel == PS_KERNEL_AUTO) kernel = bulk_shape ? PS_KERNEL_BULK : PS_KERNEL_ROWS;
@@ -1052,19 +1038,29 @@ static cudaError_t allow_smem(const void* fn, int bytes) {
   return err;
 }
 
+template <typename T, int FLAGS>
+static void launch_rows(const Plan& plan, dim3 grid, dim3 block, cudaStream_t stream) {
+  switch (plan.V) {
+    case 1: rows_kernel<T, 1, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    case 2: rows_kernel<T, 2, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    case 3: rows_kernel<T, 3, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    case 4: rows_kernel<T, 4, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    case 5: rows_kernel<T, 5, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    case 6: rows_kernel<T, 6, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    case 8: rows_kernel<T, 8, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
+    default: break;
+  }
+}
+
 template <typename T>
 static cudaError_t launch_typed(const Plan& plan, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(plan.blocks)), block(plan.threads);
   if (plan.kernel == PS_KERNEL_ROWS) {
-    switch (plan.V) {
-      case 1: rows_kernel<T, 1><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      case 2: rows_kernel<T, 2><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      case 3: rows_kernel<T, 3><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      case 4: rows_kernel<T, 4><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      case 5: rows_kernel<T, 5><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      case 6: rows_kernel<T, 6><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      case 8: rows_kernel<T, 8><<<grid, block, plan.smem, stream>>>(plan.params); break;
-      default: return cudaErrorInvalidValue;
+    switch (plan.params.flags) {
+      case kModeRing: launch_rows<T, kModeRing>(plan, grid, block, stream); break;
+      case kModeRef: launch_rows<T, kModeRef>(plan, grid, block, stream); break;
+      case kModeSink: launch_rows<T, kModeSink>(plan, grid, block, stream); break;
+      default: launch_rows<T, 0>(plan, grid, block, stream); break;
     }
     return cudaGetLastError();
   }
