@@ -368,7 +368,7 @@ def run_reference(args):
                          "cpu": cpu_model()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    emit(line)
     return 0
 
 
@@ -474,7 +474,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gpu": torch.cuda.get_device_name(device),
         }
-        print(json.dumps(line))
+        emit(line)
     if graph is not None:
         del graph
     if world > 1:
@@ -572,7 +572,7 @@ def run_pipeline(args):
             "clocks": {"per_rank": all_clocks, **all_clocks[0]},
             "gpu_launches": launches[0], "e2e": None,
         }
-        print(json.dumps(line))
+        emit(line)
     dist.destroy_process_group()
     return 0
 
@@ -613,7 +613,28 @@ def run_e2e(args, work, world, device, stream):
             "d2h_bytes_per_step": T * C * 2, "steps": steps, "api": "physisserve_b200.ops.qk_norm_rope_kv"}
 
 
+_RESULT_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the process's real stdout."""
+    out = _RESULT_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def _reserve_stdout() -> None:
+    """Keep stdout for the result line only: native libraries that print to fd 1 (NCCL's
+    version banner, for one) are sent to stderr instead."""
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
 def main(argv=None):
+    _reserve_stdout()
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)

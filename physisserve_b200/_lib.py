@@ -112,9 +112,9 @@ def load() -> ctypes.CDLL:
     lib.ps_error_message.restype = ctypes.c_char_p
     lib.ps_error_message.argtypes = []
     lib.ps_qk_prep_validate.restype = ctypes.c_int32
-    lib.ps_qk_prep_validate.argtypes = [ctypes.POINTER(PsQkPrepArgs)]
+    lib.ps_qk_prep_validate.argtypes = [ctypes.c_void_p]
     lib.ps_qk_norm_rope_kv.restype = ctypes.c_int32
-    lib.ps_qk_norm_rope_kv.argtypes = [ctypes.POINTER(PsQkPrepArgs), ctypes.c_void_p]
+    lib.ps_qk_norm_rope_kv.argtypes = [ctypes.c_void_p, ctypes.c_void_p]  # (const ps_qk_prep_args*, stream)
     lib.ps_device_timeouts.restype = ctypes.c_int32
     lib.ps_device_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
     i64p = ctypes.POINTER(ctypes.c_int64)

@@ -9,6 +9,7 @@ allocate only the outputs the reference also allocates (``torch.empty_like`` in
 from __future__ import annotations
 
 import ctypes
+import struct
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -130,20 +131,51 @@ def flat_seq(token_start: int, n_tokens: int, grid_h: int, grid_w: int, frame_of
 
 
 def _rows(t: torch.Tensor | None, C: int, name: str):
-    """(pointer, row stride, rows) of a token-major [..., C] or [..., H, D] tensor."""
+    """(pointer, row stride, rows) of a token-major [..., C] or [..., H, D] tensor.
+
+    Works on the shape/stride tuples only (no view is created): the leading dimensions must
+    collapse to one row dimension with a single stride.
+    """
     if t is None:
         return None, 0, 0
-    if t.dim() >= 2 and t.shape[-1] * t.shape[-2] == C and t.shape[-1] != C:
-        if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
-            raise PrepError(f"{name}: heads of a token must be contiguous")
-        t = t.flatten(-2)
-    if t.shape[-1] != C or t.stride(-1) != 1:
-        raise PrepError(f"{name}: last dimension must be C={C} with unit stride, got {tuple(t.shape)}")
+    shape, strides = t.shape, t.stride()
+    if len(shape) >= 2 and shape[-1] != C:
+        if shape[-1] * shape[-2] != C or strides[-1] != 1 or strides[-2] != shape[-1]:
+            raise PrepError(f"{name}: last dimensions must be [C={C}] or [H, D] with H*D=C contiguous, "
+                            f"got {tuple(shape)}")
+        shape, strides = shape[:-1], strides[:-1]
+        lead = len(shape) - 1
+    else:
+        if not shape or shape[-1] != C or strides[-1] != 1:
+            raise PrepError(f"{name}: last dimension must be C={C} with unit stride, got {tuple(t.shape)}")
+        lead = len(shape) - 1
+    rows, row_stride, expected = 1, C, None
+    for i in range(lead - 1, -1, -1):
+        n = shape[i]
+        if n == 1:
+            continue
+        if expected is None:
+            row_stride = strides[i]
+        elif strides[i] != expected:
+            raise PrepError(f"{name}: leading dimensions must collapse to one row dimension (token-major layout)")
+        expected = strides[i] * n
+        rows *= n
+    return t.data_ptr(), row_stride, rows
+
+
+# ps_qk_prep_args and ps_seq packed with struct (layout checked against include/physis_b200.h
+# by the tests): building them this way costs a few microseconds per launch, which matters
+# for the small per-block launches of a single stream.
+_ARGS = struct.Struct("=8if9iq" + "Qq" * 3 + "QQQQq" + "Qq" * 3 + "q" + "Qq" + "Q")
+_SEQ = struct.Struct("=qiiiiqqii")
+_DEVICE_DTYPES = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+
+def _current_stream(device_index: int) -> int:
     try:
-        rows = t.view(-1, C) if t.dim() != 2 else t
-    except RuntimeError:
-        raise PrepError(f"{name}: leading dimensions must collapse to one row dimension (token-major layout)") from None
-    return rows.data_ptr(), rows.stride(0), rows.shape[0]
+        return torch._C._cuda_getCurrentRawStream(device_index)
+    except AttributeError:  # older torch
+        return torch.cuda.current_stream(device_index).cuda_stream
 
 
 def qk_norm_rope_kv(
@@ -187,25 +219,37 @@ def qk_norm_rope_kv(
     ``ctas_per_sm``, ``release``, ``vstages``, ``vdepth`` for bulk) default to the library's choice.
     """
     C = heads * head_dim
-    ref = next(t for t in (q, k, v) if t is not None)
-    device = _require_cuda(q, k, v, q_weight, k_weight, cos, sin, q_out, k_out, v_out, k_pre)
-    dtype = _dtype_code(ref)
+    ref = q if q is not None else (k if k is not None else v)
+    if ref is None:
+        raise PrepError("q, k and v are all None")
+    dtype = _DEVICE_DTYPES.get(ref.dtype)
+    if dtype is None:
+        raise PrepError(f"unsupported dtype {ref.dtype}: the kernels take bfloat16 or float32")
+    if not ref.is_cuda:
+        raise PrepError("the prep kernels run on CUDA tensors only (there is no CPU path)")
+    device_index = ref.get_device()
     for name, t in (("q", q), ("k", k), ("v", v), ("q_out", q_out), ("k_out", k_out), ("v_out", v_out),
                     ("k_pre", k_pre), ("q_weight", q_weight), ("k_weight", k_weight)):
-        if t is not None and t.dtype != ref.dtype:
-            raise PrepError(f"{name} is {t.dtype}, expected {ref.dtype}")
+        if t is not None and (t.dtype is not ref.dtype or t.get_device() != device_index):
+            if not t.is_cuda:
+                raise PrepError("the prep kernels run on CUDA tensors only (there is no CPU path)")
+            raise PrepError(f"{name} is {t.dtype} on {t.device}, expected {ref.dtype} on {ref.device}")
     for name, t in (("cos", cos), ("sin", sin)):
-        if t.dtype != torch.float32:
+        if t.dtype is not torch.float32:
             raise PrepError(f"{name} must be float32")
+        if t.get_device() != device_index:
+            raise PrepError(f"{name} must be on {ref.device}")
         if t.shape[-1] != head_dim or not t.is_contiguous():
             raise PrepError(f"{name} must be contiguous with last dimension head_dim={head_dim}")
     if cos.shape != sin.shape:
         raise PrepError("cos and sin differ in shape")
-    mode = {"axes": _lib.TABLE_AXES, "tokens": _lib.TABLE_TOKENS}[table_mode]
-    if mode == _lib.TABLE_AXES:
+    if table_mode == "axes":
+        mode = _lib.TABLE_AXES
         split = tuple(axis_split) if axis_split is not None else _default_split(head_dim)
+    elif table_mode == "tokens":
+        mode, split = _lib.TABLE_TOKENS, (0, 0, 0)
     else:
-        split = (0, 0, 0)
+        raise PrepError(f"table_mode {table_mode!r} is not 'axes' or 'tokens'")
     for name, w in (("q_weight", q_weight), ("k_weight", k_weight)):
         if w is not None and (w.numel() != C or not w.is_contiguous()):
             raise PrepError(f"{name} must be a contiguous [{C}] vector")
@@ -221,26 +265,28 @@ def qk_norm_rope_kv(
                   if t is not None)
     kv_rows = min([r for r, t in ((ko_rows, k_out), (vo_rows, v_out)) if t is not None] or [0])
     table_rows = cos.numel() // head_dim
+    kern = _KERNELS.get(kernel)
+    if kern is None:
+        raise PrepError(f"kernel {kernel!r} is not 'auto', 'bulk' or 'rows'")
 
     lib = _lib.load()
-    stream = _stream(device)
+    stream = _current_stream(device_index)
+    qw = 0 if q_weight is None else q_weight.data_ptr()
+    kw = 0 if k_weight is None else k_weight.data_ptr()
     seqs = list(seqs)
     for begin in range(0, max(1, len(seqs)), _lib.MAX_SEQS):
         part = seqs[begin:begin + _lib.MAX_SEQS]
-        array = (_lib.PsSeq * len(part))(*[s.to_c() for s in part])
-        args = _lib.PsQkPrepArgs(
-            dtype=dtype, heads=heads, head_dim=head_dim, table_mode=mode,
-            t_dim=split[0], h_dim=split[1], w_dim=split[2], n_seqs=len(part), eps=float(eps),
-            heads_per_thread=heads_per_thread, kernel=_KERNELS[kernel], stages=stages, groups=groups,
-            ctas_per_sm=ctas_per_sm, row_threads=row_threads, release=release, vstages=vstages, vdepth=vdepth, in_rows=in_rows,
-            q=qp, q_stride=qs, k=kp, k_stride=ks, v=vp, v_stride=vs,
-            q_weight=None if q_weight is None else q_weight.data_ptr(),
-            k_weight=None if k_weight is None else k_weight.data_ptr(),
-            cos=cos.data_ptr(), sin=sin.data_ptr(), table_rows=table_rows,
-            q_out=qop, q_out_stride=qos, k_out=kop, k_out_stride=kos, v_out=vop, v_out_stride=vos,
-            kv_out_rows=kv_rows, k_pre=kpp, k_pre_stride=kps,
-            seqs=ctypes.cast(array, ctypes.POINTER(_lib.PsSeq)))
-        _check(lib.ps_qk_norm_rope_kv(ctypes.byref(args), stream))
+        seq_buf = ctypes.create_string_buffer(_SEQ.size * max(1, len(part)))
+        for i, sq in enumerate(part):
+            _SEQ.pack_into(seq_buf, i * _SEQ.size, sq.token_start, sq.n_tokens, sq.grid_h, sq.grid_w,
+                           sq.frame_offset, sq.table_row, sq.ring_row, sq.ring_frames, sq.ring_slot0)
+        args = ctypes.create_string_buffer(_ARGS.size)
+        _ARGS.pack_into(args, 0, dtype, heads, head_dim, mode, split[0], split[1], split[2], len(part), float(eps),
+                        heads_per_thread, kern, stages, groups, ctas_per_sm, row_threads, release, vstages, vdepth,
+                        in_rows, qp or 0, qs, kp or 0, ks, vp or 0, vs, qw, kw, cos.data_ptr(), sin.data_ptr(),
+                        table_rows, qop or 0, qos, kop or 0, kos, vop or 0, vos, kv_rows, kpp or 0, kps,
+                        ctypes.addressof(seq_buf))
+        _check(lib.ps_qk_norm_rope_kv(args, stream))
 
 
 _KERNELS = {"auto": _lib.KERNEL_AUTO, "rows": _lib.KERNEL_ROWS, "bulk": _lib.KERNEL_BULK}

@@ -6,6 +6,7 @@ import re
 import subprocess
 
 import pytest
+import torch
 
 from physisserve_b200 import _lib
 from physisserve_b200.build import INCLUDE, build
@@ -89,7 +90,7 @@ def _args(**over):
 
 
 def _validate(lib, args):
-    status = lib.ps_qk_prep_validate(ctypes.byref(args))
+    status = lib.ps_qk_prep_validate(ctypes.addressof(args))
     return status, lib.ps_error_message().decode()
 
 
@@ -166,3 +167,54 @@ def test_rope_validate(lib):
     assert bad == _lib.ERR_ALIGN
     odd = lib.ps_rope_validate(_lib.BF16, BASE, strides, BASE, BASE, tab, BASE, strides, 1, 1560, 12, 7)
     assert odd == _lib.ERR_SHAPE
+
+
+def test_packed_arguments_match_the_header_layout():
+    """ops packs ps_qk_prep_args / ps_seq with struct; the bytes equal the ctypes mirror of
+    the header (whose offsets test_struct_layout_matches_header checks against the C compiler)."""
+    from physisserve_b200 import ops
+
+    values = [3, 40, 128, 1, 44, 42, 42, 8, 1e-6, 5, 2, 7, 6, 1, 64, 3, 4, 2, 12480]
+    ptrs = [(1 << 40) + 16 * i for i in range(30)]
+    args = _lib.PsQkPrepArgs(
+        dtype=3, heads=40, head_dim=128, table_mode=1, t_dim=44, h_dim=42, w_dim=42, n_seqs=8, eps=1e-6,
+        heads_per_thread=5, kernel=2, stages=7, groups=6, ctas_per_sm=1, row_threads=64, release=3, vstages=4,
+        vdepth=2, in_rows=12480, q=ptrs[0], q_stride=5120, k=ptrs[1], k_stride=5121, v=ptrs[2], v_stride=5122,
+        q_weight=ptrs[3], k_weight=ptrs[4], cos=ptrs[5], sin=ptrs[6], table_rows=4096, q_out=ptrs[7],
+        q_out_stride=5123, k_out=ptrs[8], k_out_stride=5124, v_out=ptrs[9], v_out_stride=5125, kv_out_rows=99,
+        k_pre=ptrs[10], k_pre_stride=5126)
+    args.seqs = ctypes.cast(ctypes.c_void_p(ptrs[11]), ctypes.POINTER(_lib.PsSeq))
+    packed = ops._ARGS.pack(*values, ptrs[0], 5120, ptrs[1], 5121, ptrs[2], 5122, ptrs[3], ptrs[4], ptrs[5], ptrs[6],
+                            4096, ptrs[7], 5123, ptrs[8], 5124, ptrs[9], 5125, 99, ptrs[10], 5126, ptrs[11])
+    assert ops._ARGS.size == ctypes.sizeof(_lib.PsQkPrepArgs)
+    assert packed == bytes(args)
+    seq = _lib.PsSeq(7, 1560, 30, 52, 9, 11, 13, 12, 5)
+    assert ops._SEQ.size == ctypes.sizeof(_lib.PsSeq)
+    assert ops._SEQ.pack(7, 1560, 30, 52, 9, 11, 13, 12, 5) == bytes(seq)
+
+
+@pytest.mark.parametrize("shape,strides,rows,row_stride", [
+    ((12480, 5120), (5120, 1), 12480, 5120),
+    ((8, 1560, 5120), (1560 * 5120, 5120, 1), 12480, 5120),
+    ((8, 1560, 40, 128), (1560 * 5120, 5120, 128, 1), 12480, 5120),
+    ((1560, 5120), (3 * 5120, 1), 1560, 3 * 5120),
+    ((5120,), (1,), 1, 5120),
+    ((1, 1, 5120), (5120, 5120, 1), 1, 5120),
+])
+def test_row_view_of_tensors(shape, strides, rows, row_stride):
+    from physisserve_b200 import ops
+
+    t = torch.empty_strided(shape, strides, dtype=torch.bfloat16)
+    _, got_stride, got_rows = ops._rows(t, 5120, "t")
+    assert (got_rows, got_stride) == (rows, row_stride)
+
+
+def test_row_view_rejects_non_collapsible():
+    from physisserve_b200 import ops
+
+    t = torch.empty_strided((2, 3, 5120), (4 * 5120, 5120, 1), dtype=torch.bfloat16)
+    with pytest.raises(ops.PrepError, match="collapse"):
+        ops._rows(t, 5120, "t")
+    t = torch.empty(4, 2, 128, dtype=torch.bfloat16).transpose(0, 1)
+    with pytest.raises(ops.PrepError):
+        ops._rows(t, 256, "t")
