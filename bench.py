@@ -577,6 +577,89 @@ def run_pipeline(args):
     return 0
 
 
+def run_torch_gpu(args):
+    """The reference algorithm as PyTorch ops on the GPU, for comparison with the fused kernel:
+    F.rms_norm of Q and K over H*D (torch.nn.RMSNorm), per-token cos/sin gathered from the
+    per-axis tables (WanDiT._frames_table), the rotation as _rope evaluates it (wan.py:58-63),
+    and rotated K / V copied into each stream's ring slot.  Same workload, timing and JSON as
+    the default arm."""
+    import torch.nn.functional as F
+
+    rank, world, local = init_dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    work = Workload(args.workload, rank, world, device, ring_frames=args.ring_frames)
+    C, D, H = work.C, work.head_dim, work.heads
+    split = (D - 4 * (D // 6), 2 * (D // 6), 2 * (D // 6))
+    hw = work.hw
+    # Token -> (frame, row, col) per stream; positions move with the step's offsets.
+    local_l = torch.cat([torch.arange(n, device=device) for n in work.tokens])
+    frame_local = local_l // hw
+    hh = (local_l % hw) // work.gw
+    ww = local_l % work.gw
+    stream_of = torch.cat([torch.full((n,), i, device=device) for i, n in enumerate(work.tokens)])
+    offsets0 = torch.tensor(work.offsets, device=device)
+
+    def tables(step):
+        frame = offsets0[stream_of] + frame_local + step
+        parts = []
+        for table in (work.cos, work.sin):
+            ft, fh, fw = table.split(split, dim=1)
+            parts.append(torch.cat((ft[frame], fh[hh], fw[ww]), dim=1)[:, None, :])
+        return parts
+
+    def rope(x, cosine, sine):
+        even, odd = x.unflatten(-1, (-1, 2)).unbind(-1)
+        result = torch.empty_like(x)
+        result[..., 0::2] = even * cosine[..., 0::2] - odd * sine[..., 1::2]
+        result[..., 1::2] = even * sine[..., 0::2] + odd * cosine[..., 1::2]
+        return result
+
+    rows_base = torch.tensor([i * work.rows for i in range(len(work.tokens))], device=device)
+
+    def step(i):
+        q, k, v = work.inputs[i % len(work.inputs)]
+        cosine, sine = tables(i)
+        qn = F.rms_norm(q, (C,), work.wq[0], 1e-6).view(-1, H, D)
+        kn = F.rms_norm(k, (C,), work.wk[0], 1e-6).view(-1, H, D)
+        work.q_out.view(-1, H, D).copy_(rope(qn, cosine, sine))
+        slot = (offsets0[stream_of] + frame_local + i) % work.capacity
+        dest = rows_base[stream_of] + slot * hw + local_l % hw
+        work.ring_k.index_copy_(0, dest, rope(kn, cosine, sine).view(-1, C))
+        work.ring_v.index_copy_(0, dest, v)
+        return 1
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(device)
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    begin.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    finish.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = max_over_ranks(begin.elapsed_time(finish), world, device)
+    tokens = sum(gather_objects(work.tokens_per_launch * args.steps, world))
+    if rank == 0:
+        emit({"impl": "torch-gpu", "metric": "rotated_qk_tokens_per_s", "value": tokens / (ms / 1000.0),
+              "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+              "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+              "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+              "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"],
+                         "path": "reference algorithm as PyTorch ops on the GPU (one block call per step)"},
+              "clocks": clocks})
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
 def run_e2e(args, work, world, device, stream):
     """The public API end to end: H2D of q, k, v from pinned host memory, the fused prep
     through physisserve_b200.ops.qk_norm_rope_kv, D2H of the rotated Q (every step)."""
@@ -639,7 +722,9 @@ def main(argv=None):
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
-    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--impl", choices=("ours", "reference", "torch"), default="ours",
+                        help="ours: the fused kernels; reference: the reference algorithm on host CPU cores; "
+                             "torch: the reference algorithm as PyTorch ops on the GPU")
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3")
     parser.add_argument("--graph", action="store_true", help="replay each step from a captured CUDA graph")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -667,6 +752,8 @@ def main(argv=None):
         return run_reference(args)
     if args.pipeline:
         return run_pipeline(args)
+    if args.impl == "torch":
+        return run_torch_gpu(args)
     return run_ours(args)
 
 

@@ -492,6 +492,42 @@ def test_prepare_reference_layout_batch_members(golden):
                          f"batch page {m}")
 
 
+def test_ring_attention_processor_output_matches_reference(golden):
+    """RingAttention over the recorded request: the block's attention output equals the
+    reference _Attention's (keys in ring order only change SDPA's summation order)."""
+    g = golden("attention.pt")
+    heads, D = g["heads"], g["head_dim"]
+    gh, gw = g["grid"]
+    attn = _attn(g)
+    from physisserve_b200.wan import RingAttention
+    processor = RingAttention()
+    processor.cache = RingCache(heads=heads, head_dim=D, grid_h=gh, grid_w=gw, device=DEV)
+    cos, sin = g["freqs_cos"].to(DEV), g["freqs_sin"].to(DEV)
+    records = {r["chunk"]: r for r in g["records"]}
+    for chunk, inputs in enumerate(g["inputs"]):
+        for name in ("q", "k", "v"):
+            getattr(attn, f"to_{name}").value = inputs[name].to(DEV)
+        with torch.inference_mode():
+            out = processor(attn, torch.empty(1, device=DEV), rotary_emb=(cos, sin, [window_layout(chunk)]))
+        rec = records.get(chunk)
+        if rec is not None:
+            torch.testing.assert_close(out.float().cpu(), rec["out"].float(), atol=3e-2, rtol=3e-2)
+
+
+def test_more_sequences_than_one_launch_holds():
+    """100 streams in one call: the wrapper splits them into launches of at most 64."""
+    H, D, gh, gw, capacity = 2, 128, 2, 3, 4
+    C, hw, B = H * D, 6, 100
+    q, k, v = (randn((B, hw, C), s) for s in (81, 82, 83))
+    wq, wk = norm_weight(C, 84), norm_weight(C, 85)
+    cos, sin = oracle.rope_tables(D, 256)
+    split = oracle.axis_dims(D)
+    offsets = [3 + (7 * b) % 150 for b in range(B)]
+    slots = [o % capacity for o in offsets]
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True)
+    _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
+
+
 def test_no_bounded_wait_ran_out():
     """After every kernel above, the bulk kernel's bounded mbarrier waits never expired."""
     assert ops.device_timeouts(reset=True) == 0
