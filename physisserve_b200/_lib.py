@@ -88,14 +88,6 @@ class PsQkPrepArgs(ctypes.Structure):
     ]
 
 
-class NativeError(RuntimeError):
-    """A non-zero ``ps_status`` from the native library."""
-
-    def __init__(self, status: int, message: str):
-        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
-        self.status = status
-
-
 _LIB = None
 
 
@@ -129,13 +121,6 @@ def load() -> ctypes.CDLL:
         raise ImportError(f"{LIB_PATH} has ABI version {version}, expected {ABI_VERSION}")
     _LIB = lib
     return lib
-
-
-def check(status: int) -> None:
-    """Raise ``NativeError`` (a ValueError-like failure) for a non-zero status."""
-    if status != OK:
-        message = load().ps_error_message().decode(errors="replace")
-        raise NativeError(status, message)
 
 
 def int64_array(values) -> ctypes.Array:

@@ -3,8 +3,8 @@
 Tensors are passed to the C ABI as raw device pointers plus element strides; every
 launch goes on the current CUDA stream of the tensors' device.  These wrappers
 allocate only the outputs the reference also allocates (``torch.empty_like`` in
-``_rope``, wan.py:60); all validation errors surface as ``ValueError``
-(``NativeError``) carrying the library's message.
+``_rope``, wan.py:60); all validation errors surface as ``PrepError`` (a
+``ValueError``) carrying the library's status name and message.
 """
 from __future__ import annotations
 

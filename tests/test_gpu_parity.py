@@ -528,6 +528,51 @@ def test_more_sequences_than_one_launch_holds():
     _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
 
 
+def test_drop_in_processor_block_batch(golden):
+    """Attention under WanDiT.block_batch's protocol: two members with stacked own/window
+    tables and a BatchCache, against the reference's recorded batch call."""
+    g = golden("attention.pt")
+    b = g["batch"]
+    heads, D = g["heads"], g["head_dim"]
+    attn = _attn(g)
+    pages = {}
+    for chunk, inputs in enumerate(g["inputs"]):
+        kn = oracle.rms_norm(inputs["k"], g["norm_k_weight"], g["eps"]).unflatten(2, (heads, -1)).transpose(1, 2)
+        pages[chunk] = (kn.to(DEV), inputs["v"].unflatten(2, (heads, -1)).transpose(1, 2).to(DEV))
+    caches = [oracle.Cache([pages[p] for p in oracle.history_chunks(c)]) for c in b["members"]]
+    processor = Attention()
+    processor.cache = oracle.BatchCache(caches, 1)
+    for name in ("q", "k", "v"):
+        getattr(attn, f"to_{name}").value = b[name].to(DEV)
+    own = tuple(t.to(DEV) for t in b["own"])
+    window = tuple(t.to(DEV) for t in b["window"])
+    captured = {}
+    import physisserve_b200.wan as wan_mod
+    original = wan_mod.F.scaled_dot_product_attention
+
+    def spy(q, k, v, *a, **kw):
+        captured["sdpa"] = (q, k, v)
+        return original(q, k, v, *a, **kw)
+
+    wan_mod.F.scaled_dot_product_attention = spy
+    try:
+        with torch.inference_mode():
+            out = processor(attn, torch.empty(1, device=DEV), rotary_emb=(own, window))
+    finally:
+        wan_mod.F.scaled_dot_product_attention = original
+    q_rot, k_rot, v_win = (t.cpu() for t in captured["sdpa"])
+    normed_q = _normed_heads(b["q"], g["norm_q_weight"], g["eps"], heads)
+    check_rotated_close(q_rot, b["q_rot"], normed_q, "batch Q'")
+    normed_windows = torch.cat([torch.cat([pages[p][0].cpu() for p in oracle.history_chunks(c)] +
+                                          [_normed_heads(b["k"][m:m + 1], g["norm_k_weight"], g["eps"], heads)], dim=2)
+                                for m, c in enumerate(b["members"])])
+    check_rotated_close(k_rot, b["k_window_rot"], normed_windows, "batch K window'")
+    assert torch.equal(v_win, b["v_window"])
+    for m, cache in enumerate(caches):
+        check_bf16_close(cache.page[0].contiguous().cpu(), b["pages_k"][m], f"member {m} page")
+    torch.testing.assert_close(out.float().cpu(), b["out"].float(), atol=3e-2, rtol=3e-2)
+
+
 def test_no_bounded_wait_ran_out():
     """After every kernel above, the bulk kernel's bounded mbarrier waits never expired."""
     assert ops.device_timeouts(reset=True) == 0

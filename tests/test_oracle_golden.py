@@ -188,3 +188,25 @@ def test_window_positions_cover_history(chunk):
     for (page, frame), (_, nxt) in zip(positions, positions[1:]):
         assert nxt - frame == geometry.frames_of(page)
     assert positions[-1][1] == geometry.start(chunk)
+
+
+def test_batch_cache_matches_reference(golden):
+    """The oracle's BatchCache packs the members' windows exactly as the reference's did, and
+    the window RoPE with the stacked tables gives the recorded rotated window."""
+    g = golden("attention.pt")
+    heads, eps = g["heads"], g["eps"]
+    wk = g["norm_k_weight"]
+    pages = {}
+    for chunk, inputs in enumerate(g["inputs"]):
+        kn = oracle.rms_norm(inputs["k"], wk, eps).unflatten(2, (heads, -1)).transpose(1, 2)
+        pages[chunk] = (kn, inputs["v"].unflatten(2, (heads, -1)).transpose(1, 2))
+    b = g["batch"]
+    caches = [oracle.Cache([pages[p] for p in oracle.history_chunks(c)]) for c in b["members"]]
+    k = oracle.rms_norm(b["k"], wk, eps).unflatten(2, (heads, -1)).transpose(1, 2)
+    v = b["v"].unflatten(2, (heads, -1)).transpose(1, 2)
+    kw, vw = oracle.BatchCache(caches, 1)(k, v)
+    k_rot = oracle.rope(kw.transpose(1, 2), *b["window"]).type_as(kw).transpose(1, 2)
+    assert torch.equal(k_rot, b["k_window_rot"])
+    assert torch.equal(vw, b["v_window"])
+    for m, cache in enumerate(caches):
+        assert torch.equal(cache.page[0].contiguous(), b["pages_k"][m])
