@@ -660,6 +660,127 @@ def run_torch_gpu(args):
     return 0
 
 
+def run_processor(args):
+    """One Wan2.1-1.3B self-attention block call at steady state (chunk 25: a 22-frame window
+    of sink + 18 recent chunks + the chunk), timed for three processors on the GPU:
+
+    * ``torch``     -- the reference algorithm in PyTorch ops: RMSNorm, pre-RoPE pages,
+                       window concat (Cache, kv_cache.py:51-56), _rope of Q and of the whole
+                       window (wan.py:102-111), SDPA;
+    * ``reference`` -- physisserve_b200.wan.Attention, the drop-in with the same layout
+                       (fused RMSNorm+RoPE(Q)+page kernel, window concat, strided window RoPE);
+    * ``ring``      -- physisserve_b200.wan.RingAttention: one fused launch writes rotated K
+                       and V at their ring slot, the sink is re-rotated at its moved position,
+                       SDPA reads the ring in place (no concat, no window re-rotation).
+
+    Projections and SDPA are the same library calls in all three (bf16 Linear / torch SDPA).
+    """
+    import torch.nn.functional as F
+    from torch import nn
+
+    from physisserve_b200.wan import Attention, RingAttention, RingCache, wan_rope_tables, window_layout
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    H, D, gh, gw = 12, 128, 30, 52
+    C, hw = H * D, gh * gw
+    chunk = 25
+    g = torch.Generator().manual_seed(3)
+
+    attn = nn.Module()
+    attn.heads = H
+    attn.to_q, attn.to_k, attn.to_v = (nn.Linear(C, C) for _ in range(3))
+    attn.norm_q, attn.norm_k = nn.RMSNorm(C, eps=1e-6), nn.RMSNorm(C, eps=1e-6)
+    attn.to_out = nn.ModuleList([nn.Linear(C, C), nn.Identity()])
+    attn = attn.to(device, torch.bfloat16).eval()
+    hidden = torch.randn(1, hw, C, generator=g).bfloat16().to(device)
+    cos, sin = wan_rope_tables(D, 64, device=device)
+    split = (D - 4 * (D // 6), 2 * (D // 6), 2 * (D // 6))
+
+    # Reference layout: 19 history pages (sink chunk 0 of 3 frames + chunks 7..24), pre-RoPE.
+    pos = window_layout(chunk)
+    history = [chunk_id for chunk_id in [0, *range(chunk - 18, chunk)]]
+    frames = {c: (3 if c == 0 else 1) for c in history}
+    pages = [tuple(torch.randn(1, H, frames[c] * hw, D, generator=g).bfloat16().to(device) for _ in range(2))
+             for c in history]
+
+    def frames_table(start, stop):
+        out = []
+        for table in (cos, sin):
+            ft, fh, fw = table.split(split, dim=1)
+            n = stop - start
+            out.append(torch.cat((ft[start:stop, None, None].expand(n, gh, gw, -1),
+                                  fh[None, :gh, None].expand(n, gh, gw, -1),
+                                  fw[None, None, :gw].expand(n, gh, gw, -1)), dim=-1).reshape(1, n * hw, 1, -1))
+        return tuple(out)
+
+    own = frames_table(pos.frame_offset, pos.frame_offset + 1)
+    window = frames_table(pos.sink_position, pos.frame_offset + 1)
+
+    class Cache:
+        def __init__(self, hist):
+            self.history, self.page = hist, None
+
+        def __call__(self, key, value):
+            self.page = (key, value)
+            parts = [*self.history, (key, value)]
+            return tuple(torch.cat([p[i] for p in parts], dim=2) for i in (0, 1))
+
+    def rope(x, cosine, sine):
+        even, odd = x.unflatten(-1, (-1, 2)).unbind(-1)
+        result = torch.empty_like(x)
+        result[..., 0::2] = even * cosine[..., 0::2] - odd * sine[..., 1::2]
+        result[..., 1::2] = even * sine[..., 0::2] + odd * cosine[..., 1::2]
+        return result
+
+    def torch_processor():
+        q = attn.norm_q(attn.to_q(hidden)).unflatten(2, (H, -1))
+        k = attn.norm_k(attn.to_k(hidden)).unflatten(2, (H, -1)).transpose(1, 2)
+        v = attn.to_v(hidden).unflatten(2, (H, -1)).transpose(1, 2)
+        k, v = Cache(pages)(k, v)
+        q = rope(q, *own).type_as(q).transpose(1, 2)
+        k = rope(k.transpose(1, 2), *window).type_as(k).transpose(1, 2)
+        out = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).flatten(2)
+        return attn.to_out[1](attn.to_out[0](out))
+
+    drop_in = Attention()
+
+    def reference_processor():
+        drop_in.cache = Cache(pages)
+        return drop_in(attn, hidden, rotary_emb=(own, window))
+
+    ring = RingAttention()
+    ring.cache = RingCache(heads=H, head_dim=D, grid_h=gh, grid_w=gw, device=device)
+    ring.cache.k.normal_()
+    ring.cache.v.normal_()
+    ring.cache.sink_k.normal_()
+
+    def ring_processor():
+        ring.cache.sink_at = [pos.sink_position - 1]  # the sink moved by one frame since the last chunk
+        return ring(attn, hidden, rotary_emb=(cos, sin, [pos]))
+
+    results = {}
+    with torch.inference_mode():
+        for name, fn in (("torch", torch_processor), ("reference", reference_processor), ("ring", ring_processor)):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            begin.record()
+            for _ in range(args.steps):
+                fn()
+            finish.record()
+            torch.cuda.synchronize()
+            results[name] = begin.elapsed_time(finish) / args.steps
+    emit({"impl": "processor", "metric": "block_call_ms", "unit": "ms", "higher_is_better": False,
+          "value": results["ring"], "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+          "config": {"workload": "wan2.1-1.3b self-attention block call, chunk 25 (22-frame window)",
+                     "tokens": hw, "window_tokens": 22 * hw},
+          "ms_per_call": results, "speedup_vs_torch": {k: results["torch"] / v for k, v in results.items()},
+          "gpu": torch.cuda.get_device_name(device)})
+    return 0
+
+
 def run_e2e(args, work, world, device, stream):
     """The public API end to end: every step copies its q, k, v from pinned host memory to the
     device, runs the fused prep through physisserve_b200.ops.qk_norm_rope_kv and copies the
@@ -774,6 +895,8 @@ def main(argv=None):
     parser.add_argument("--vstages", type=int, default=0, help="bulk kernel: V stages per CTA (0 = auto)")
     parser.add_argument("--vdepth", type=int, default=0, help="bulk kernel: V stores in flight (0 = auto)")
     parser.add_argument("--cells", type=int, default=0, help="launches per step override (profiling runs)")
+    parser.add_argument("--processor", action="store_true",
+                        help="time one whole self-attention block call: torch ops vs drop-in vs ring layout")
     parser.add_argument("--pipeline", action="store_true",
                         help="BASELINE config 5 pipelined: 2-stage pipelines (15 blocks per GPU) over NCCL")
     args = parser.parse_args(argv)
@@ -783,6 +906,8 @@ def main(argv=None):
         return run_reference(args)
     if args.pipeline:
         return run_pipeline(args)
+    if args.processor:
+        return run_processor(args)
     if args.impl == "torch":
         return run_torch_gpu(args)
     return run_ours(args)
