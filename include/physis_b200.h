@@ -12,7 +12,8 @@
  * stream passed as `void*` (a cudaStream_t; NULL is the legacy default stream).
  * Arguments are validated on the host before any CUDA call; a non-zero return
  * is a ps_status and ps_error_message() describes it.  No entry point
- * allocates device memory or synchronises the stream.
+ * allocates device memory; all but ps_device_timeouts are asynchronous on the
+ * given stream.
  *
  * Layout conventions
  *   - Activations are token-major rows of C = heads*head_dim elements

@@ -35,6 +35,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "ps_common.cuh"
 
 namespace ps {
@@ -1028,9 +1030,11 @@ static cudaError_t allow_smem(const void* fn, int bytes) {
   };
   static Entry cache[64];
   static int used = 0;
+  static std::mutex lock;
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> guard(lock);
   for (int i = 0; i < used; ++i)
     if (cache[i].fn == fn && cache[i].device == dev && cache[i].bytes >= bytes) return cudaSuccess;
   err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

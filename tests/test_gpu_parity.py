@@ -573,6 +573,63 @@ def test_drop_in_processor_block_batch(golden):
     torch.testing.assert_close(out.float().cpu(), b["out"].float(), atol=3e-2, rtol=3e-2)
 
 
+@pytest.mark.parametrize("kernel", ["bulk", "rows"])
+def test_wide_rows_c8192(kernel):
+    """C = 64 x 128 = 8192 (16 KB bf16 rows): the bulk kernel's stages hold 32 KB each."""
+    H, D, gh, gw = 64, 128, 4, 6
+    C = H * D
+    B, frames, capacity = 3, 2, 3
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s) for s in (91, 92, 93))
+    wq, wk = norm_weight(C, 94), norm_weight(C, 95)
+    cos, sin = oracle.rope_tables(D, 64)
+    split = oracle.axis_dims(D)
+    offsets, slots = [4, 11, 30], [1, 2, 0]
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, k_pre=True,
+                    kernel=kernel)
+    _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
+
+
+@pytest.mark.parametrize("heads,head_dim,row_threads", [(3, 64, 32), (3, 64, 64), (1, 128, 32), (2, 16, 32),
+                                                        (5, 32, 96)])
+def test_bulk_kernel_row_tails(heads, head_dim, row_threads):
+    """Bulk kernel on rows with fewer (or not a multiple of) 16-byte vectors than the row
+    group has threads: the per-thread loop's tail is predicated."""
+    gh, gw = 3, 4
+    C = heads * head_dim
+    B, frames, capacity = 2, 2, 3
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s) for s in (101, 102, 103))
+    wq, wk = norm_weight(C, 104), norm_weight(C, 105)
+    cos, sin = oracle.rope_tables(head_dim, 32)
+    split = oracle.axis_dims(head_dim)
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), [5, 9], capacity, [1, 2], heads, head_dim,
+                    k_pre=True, kernel="bulk", row_threads=row_threads)
+    _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), [5, 9], capacity, [1, 2], heads, head_dim, got)
+
+
+@pytest.mark.parametrize("kernel", ["bulk", "rows"])
+def test_fp32_wide_rows(kernel):
+    """fp32 with C = 2048 (8 KB rows): both kernels, per-axis tables, ring writes."""
+    H, D, gh, gw = 16, 128, 3, 5
+    C = H * D
+    B, frames, capacity = 2, 1, 2
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s, torch.float32) for s in (111, 112, 113))
+    wq, wk = norm_weight(C, 114, torch.float32), norm_weight(C, 115, torch.float32)
+    cos, sin = oracle.rope_tables(D, 32)
+    split = oracle.axis_dims(D)
+    q_out, ring_k, ring_v, _ = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), [3, 7], capacity, [1, 0], H, D,
+                                         dtype=torch.float32, kernel=kernel)
+    for b, (offset, slot) in enumerate(((3, 1), (7, 0))):
+        ct, st = token_tables(cos, sin, split, offset, frames, gh, gw)
+        for got, x, w in ((q_out[b], q[b], wq), (ring_k[b, slot * L:(slot + 1) * L], k[b], wk)):
+            ref = oracle.rope(oracle.rms_norm(x, w, EPS).unflatten(-1, (H, D)), ct[:, None], st[:, None]).flatten(-2)
+            err = (got.double() - ref.double()).abs()
+            assert bool((err <= 8 * 2.0 ** -24 * pair_magnitude(ref) + 1e-30).all())
+        assert torch.equal(ring_v[b, slot * L:(slot + 1) * L], v[b])
+
+
 def test_no_bounded_wait_ran_out():
     """After every kernel above, the bulk kernel's bounded mbarrier waits never expired."""
     assert ops.device_timeouts(reset=True) == 0
