@@ -781,6 +781,43 @@ def run_processor(args):
     return 0
 
 
+def run_rope_window(args):
+    """ps_rope (the _rope drop-in) on the reference layout's K window at steady state: a
+    [1, 12, 34320, 128] bf16 window (22 frames of a 1.3B stream) rotated through its transposed
+    [1, 34320, 12, 128] view with per-token fp32 tables [1, 34320, 1, 128] (wan.py:109).
+    Algorithmic bytes: read x + write out (2 x 2 bytes per element) + the tables once
+    (2 x 4 bytes per table element)."""
+    from physisserve_b200.ops import rope
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    H, D, W = 12, 128, 22 * 1560
+    g = torch.Generator().manual_seed(11)
+    sets = [torch.randn(1, H, W, D, generator=g).bfloat16().to(device) for _ in range(2)]
+    cos = torch.rand(1, W, 1, D, generator=g).to(device)
+    sin = torch.rand(1, W, 1, D, generator=g).to(device)
+    outs = [torch.empty_like(x.transpose(1, 2)) for x in sets]
+    for i in range(args.warmup):
+        rope(sets[i % 2].transpose(1, 2), cos, sin, out=outs[i % 2])
+    torch.cuda.synchronize()
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record()
+    for i in range(args.steps):
+        rope(sets[i % 2].transpose(1, 2), cos, sin, out=outs[i % 2])
+    finish.record()
+    torch.cuda.synchronize()
+    us = 1000 * begin.elapsed_time(finish) / args.steps
+    algorithmic = 2 * 2 * H * W * D + 2 * 4 * W * D
+    peak, src = measured_peak()
+    achieved = algorithmic / (us * 1e-6) / 1e9
+    emit({"impl": "rope-window", "metric": "rotated_window_tokens_per_s", "unit": "tokens/s",
+          "value": W / (us * 1e-6), "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+          "config": {"workload": "1.3B K window [1, 34320, 12, 128] bf16 (transposed view), per-token tables"},
+          "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                       "bytes_per_launch": algorithmic, "launch_us": us, "peak_source": src}})
+    return 0
+
+
 def run_e2e(args, work, world, device, stream):
     """The public API end to end: every step copies its q, k, v from pinned host memory to the
     device, runs the fused prep through physisserve_b200.ops.qk_norm_rope_kv and copies the
@@ -895,6 +932,8 @@ def main(argv=None):
     parser.add_argument("--vstages", type=int, default=0, help="bulk kernel: V stages per CTA (0 = auto)")
     parser.add_argument("--vdepth", type=int, default=0, help="bulk kernel: V stores in flight (0 = auto)")
     parser.add_argument("--cells", type=int, default=0, help="launches per step override (profiling runs)")
+    parser.add_argument("--rope-window", action="store_true",
+                        help="time ps_rope on the reference layout's 22-frame K window")
     parser.add_argument("--processor", action="store_true",
                         help="time one whole self-attention block call: torch ops vs drop-in vs ring layout")
     parser.add_argument("--pipeline", action="store_true",
@@ -908,6 +947,8 @@ def main(argv=None):
         return run_pipeline(args)
     if args.processor:
         return run_processor(args)
+    if args.rope_window:
+        return run_rope_window(args)
     if args.impl == "torch":
         return run_torch_gpu(args)
     return run_ours(args)

@@ -174,4 +174,15 @@ __device__ __forceinline__ void rotate_pair(float e, float o, float cos_e, float
   out_o = __fadd_rn(__fmul_rn(e, sin_e), __fmul_rn(o, cos_o));
 }
 
+// The same rotation on packed operands: pair (e, o) with cos pair (cos[2i], cos[2i+1])
+// and sin pair (sin[2i], sin[2i+1]); two packed products and two scalar adds, the
+// three roundings of _rope per output.
+__device__ __forceinline__ void rotate_f2(f32x2 x, f32x2 c, f32x2 sn, float& lo, float& hi) {
+  float m1e, m1o, m2e, m2o;
+  f2_split(f2_mul(x, c), m1e, m1o);   // (e*cos[2i], o*cos[2i+1])
+  f2_split(f2_mul(x, sn), m2e, m2o);  // (e*sin[2i], o*sin[2i+1])
+  lo = __fsub_rn(m1e, m2o);
+  hi = __fadd_rn(m1o, m2e);
+}
+
 }  // namespace ps

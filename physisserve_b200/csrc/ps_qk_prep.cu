@@ -201,17 +201,6 @@ constexpr int kModeRing = kHasQ | kHasK | kHasV | kNormQ | kNormK | kKOut;  // r
 constexpr int kModeRef = kHasQ | kHasK | kNormQ | kNormK | kKPre;           // reference-layout prep
 constexpr int kModeSink = kHasK | kKOut;                                    // sink re-rotation
 
-// The rotation of one pair (e, o) with cos pair (cos[2i], cos[2i+1]) and sin pair
-// (sin[2i], sin[2i+1]): two packed products and two scalar adds, the three roundings of
-// _rope per output (wan.py:61-62).
-__device__ __forceinline__ void rotate_f2(f32x2 x, f32x2 c, f32x2 sn, float& lo, float& hi) {
-  float m1e, m1o, m2e, m2o;
-  f2_split(f2_mul(x, c), m1e, m1o);   // (e*cos[2i], o*cos[2i+1])
-  f2_split(f2_mul(x, sn), m2e, m2o);  // (e*sin[2i], o*sin[2i+1])
-  lo = __fsub_rn(m1e, m2o);
-  hi = __fadd_rn(m1o, m2e);
-}
-
 template <typename T, int V, int FLAGS>
 __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant__ KParams p) {
   using PT = Pairs16<T>;

@@ -3,73 +3,93 @@
 // Used where the reference layout must be kept exactly: the window RoPE of
 // _Attention (wan.py:109), whose input is the transposed view
 // [B, window_tokens, H, D] of the concatenated pre-RoPE K window, and the Q
-// RoPE with per-token tables.  Each thread rotates two 16-byte vectors (8
-// bf16 or 4 fp32 elements each); the three outer dimensions are visited in
-// the order of decreasing x stride so that consecutive threads touch
-// consecutive memory for any permutation of [B, L, H].
+// RoPE with per-token tables.  The tables depend on the token (b, l) only, so
+// a thread owns one 16-byte slice (8 bf16 or 4 fp32 elements) of one token and
+// walks up to kMaxHeads heads with it: the cos/sin slice is loaded once per
+// token and head chunk instead of once per head, all of the chunk's x loads are
+// in flight before the first rotation, and the only divisions are two
+// magic-number ones per thread.  Consecutive threads cover consecutive slices of
+// a token, then consecutive tokens, so every warp reads and writes whole
+// head rows for any strides of [B, L, H].
 
 #include "ps_common.cuh"
 
 namespace ps {
 namespace {
 
-constexpr int kVecsPerThread = 2;
+constexpr int kThreads = 256;
+constexpr int kMaxHeads = 8;  // heads one thread rotates (the chunk along H)
+
+int sm_count() {
+  static int cached = 0;
+  if (cached > 0) return cached;
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      n > 0)
+    cached = n;
+  return n > 0 ? n : 148;
+}
 
 struct RopeParams {
   const void* x;
   const float* cos;
   const float* sin;
   void* out;
-  int64_t n[3];        // outer dimension sizes, outermost first
-  int64_t xs[3];       // x element strides of those dimensions
-  int64_t os[3];       // out element strides
-  int64_t ts[3];       // table element strides (0 for the head dimension)
-  int64_t total_vecs;  // n0*n1*n2*vph
-  int32_t vph;         // 16-byte vectors per head
+  int64_t xb, xl, xh;  // x element strides of B, L, H
+  int64_t ob, ol, oh;  // out element strides
+  int64_t tb, tl;      // table element strides of B, L (H broadcasts)
+  uint64_t vph_magic;  // division by vph
+  uint64_t l_magic;    // division by L
+  uint32_t vph;        // 16-byte slices per head
+  uint32_t L;
+  uint32_t tokens;     // B * L
+  int32_t heads;
+  int32_t heads_per_block;  // chunk of H one blockIdx.y covers (<= kMaxHeads)
 };
 
 template <typename T>
-__global__ void __launch_bounds__(256) rope_kernel(const __grid_constant__ RopeParams p) {
-  using VT = Vec16<T>;
-  constexpr int E = VT::kElems;
-  constexpr int P = E / 2;
-  const int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * kVecsPerThread;
+__global__ void __launch_bounds__(kThreads, 4) rope_kernel(const __grid_constant__ RopeParams p) {
+  using PT = Pairs16<T>;
+  constexpr int E = Vec16<T>::kElems;
+  constexpr int P = PT::kPairs;
+  const uint32_t gid = blockIdx.x * kThreads + threadIdx.x;
+  const uint32_t token = div_by(gid, p.vph_magic);
+  if (token >= p.tokens) return;
+  const uint32_t dv = gid - token * p.vph;
+  const uint32_t b = div_by(token, p.l_magic);
+  const uint32_t l = token - b * p.L;
+  const int h0 = blockIdx.y * p.heads_per_block;
+  const int nh = min(p.heads - h0, p.heads_per_block);
+  const int64_t e0 = static_cast<int64_t>(dv) * E;
 
-  uint4 xv[kVecsPerThread];
-  int64_t xo[kVecsPerThread], oo[kVecsPerThread], to[kVecsPerThread];
-  bool ok[kVecsPerThread];
+  const T* xp = static_cast<const T*>(p.x) + b * p.xb + l * p.xl + h0 * p.xh + e0;
+  uint4 xv[kMaxHeads];
 #pragma unroll
-  for (int u = 0; u < kVecsPerThread; ++u) {
-    const int64_t idx = base + u;
-    ok[u] = idx < p.total_vecs;
-    const int64_t id = ok[u] ? idx : 0;
-    const int64_t dv = id % p.vph;
-    int64_t rest = id / p.vph;
-    const int64_t i2 = rest % p.n[2];
-    rest /= p.n[2];
-    const int64_t i1 = rest % p.n[1];
-    const int64_t i0 = rest / p.n[1];
-    xo[u] = i0 * p.xs[0] + i1 * p.xs[1] + i2 * p.xs[2] + dv * E;
-    oo[u] = i0 * p.os[0] + i1 * p.os[1] + i2 * p.os[2] + dv * E;
-    to[u] = i0 * p.ts[0] + i1 * p.ts[1] + i2 * p.ts[2] + dv * E;
-    if (ok[u]) xv[u] = ld_stream(static_cast<const T*>(p.x) + xo[u]);
+  for (int u = 0; u < kMaxHeads; ++u)
+    if (u < nh) xv[u] = ld_stream(xp + u * p.xh);
+
+  const int64_t t0 = b * p.tb + l * p.tl + e0;
+  f32x2 c[P], sn[P];
+#pragma unroll
+  for (int e = 0; e < E; e += 4) {
+    const float4 cv = __ldg(reinterpret_cast<const float4*>(p.cos + t0 + e));
+    const float4 sv = __ldg(reinterpret_cast<const float4*>(p.sin + t0 + e));
+    c[e / 2] = f2_make(cv.x, cv.y);
+    c[e / 2 + 1] = f2_make(cv.z, cv.w);
+    sn[e / 2] = f2_make(sv.x, sv.y);
+    sn[e / 2 + 1] = f2_make(sv.z, sv.w);
   }
+
+  T* op = static_cast<T*>(p.out) + b * p.ob + l * p.ol + h0 * p.oh + e0;
 #pragma unroll
-  for (int u = 0; u < kVecsPerThread; ++u) {
-    if (!ok[u]) continue;
-    float c[E], s[E], x[E], y[E];
+  for (int u = 0; u < kMaxHeads; ++u) {
+    if (u >= nh) break;
+    f32x2 x[P];
+    float lo[P], hi[P];
+    PT::unpack(xv[u], x);
 #pragma unroll
-    for (int e = 0; e < E; e += 4) {
-      const float4 cv = __ldg(reinterpret_cast<const float4*>(p.cos + to[u] + e));
-      const float4 sv = __ldg(reinterpret_cast<const float4*>(p.sin + to[u] + e));
-      c[e] = cv.x; c[e + 1] = cv.y; c[e + 2] = cv.z; c[e + 3] = cv.w;
-      s[e] = sv.x; s[e + 1] = sv.y; s[e + 2] = sv.z; s[e + 3] = sv.w;
-    }
-    VT::unpack(xv[u], x);
-#pragma unroll
-    for (int j = 0; j < P; ++j)
-      rotate_pair(x[2 * j], x[2 * j + 1], c[2 * j], c[2 * j + 1], s[2 * j], s[2 * j + 1], y[2 * j], y[2 * j + 1]);
-    st_vec(static_cast<T*>(p.out) + oo[u], VT::pack(y));
+    for (int j = 0; j < P; ++j) rotate_f2(x[j], c[j], sn[j], lo[j], hi[j]);
+    st_vec(op + u * p.oh, PT::pack(lo, hi));
   }
 }
 
@@ -93,32 +113,30 @@ static int build(int32_t dtype, const void* x, const int64_t* x_strides, const f
   }
   if (tab_strides[0] < 0 || tab_strides[1] < 0 || (tab_strides[0] * 4) % 16 || (tab_strides[1] * 4) % 16)
     return fail(PS_ERR_ALIGN, "table strides must be non-negative multiples of 16 bytes");
-  // Order the outer dimensions by decreasing x stride (stable).
-  int64_t n[3] = {B, L, H};
-  int64_t xs[3] = {x_strides[0], x_strides[1], x_strides[2]};
-  int64_t os[3] = {out_strides[0], out_strides[1], out_strides[2]};
-  int64_t ts[3] = {tab_strides[0], tab_strides[1], 0};
-  for (int i = 0; i < 3; ++i)
-    for (int j = 0; j + 1 < 3 - i; ++j)
-      if (xs[j] < xs[j + 1]) {
-        int64_t t;
-        t = n[j]; n[j] = n[j + 1]; n[j + 1] = t;
-        t = xs[j]; xs[j] = xs[j + 1]; xs[j + 1] = t;
-        t = os[j]; os[j] = os[j + 1]; os[j + 1] = t;
-        t = ts[j]; ts[j] = ts[j + 1]; ts[j + 1] = t;
-      }
-  for (int i = 0; i < 3; ++i) {
-    p->n[i] = n[i] > 0 ? n[i] : 1;
-    p->xs[i] = xs[i];
-    p->os[i] = os[i];
-    p->ts[i] = ts[i];
-  }
+  const int64_t vph = D / E;
+  const int64_t tokens = B * L;
+  if (tokens > 0xffffffffLL || tokens * vph > 0xfffffe00LL || L > 0xffffffffLL || H > 0x7fffffffLL)
+    return fail(PS_ERR_UNSUPPORTED, "shape [%lld,%lld,%lld,%lld] exceeds 32-bit thread indexing", (long long)B,
+                (long long)L, (long long)H, (long long)D);
   p->x = x;
   p->cos = cos;
   p->sin = sin;
   p->out = out;
-  p->vph = static_cast<int32_t>(D / E);
-  p->total_vecs = (B > 0 && L > 0 && H > 0) ? B * L * H * (D / E) : 0;
+  p->xb = x_strides[0];
+  p->xl = x_strides[1];
+  p->xh = x_strides[2];
+  p->ob = out_strides[0];
+  p->ol = out_strides[1];
+  p->oh = out_strides[2];
+  p->tb = tab_strides[0];
+  p->tl = tab_strides[1];
+  p->vph = static_cast<uint32_t>(vph);
+  p->vph_magic = div_magic(static_cast<uint32_t>(vph));
+  p->L = static_cast<uint32_t>(L > 0 ? L : 1);
+  p->l_magic = div_magic(p->L);
+  p->tokens = (B > 0 && L > 0 && H > 0) ? static_cast<uint32_t>(tokens) : 0;
+  p->heads = static_cast<int32_t>(H);
+  p->heads_per_block = 1;
   *es_out = es;
   return PS_OK;
 }
@@ -141,16 +159,27 @@ extern "C" int32_t ps_rope(int32_t dtype, const void* x, const int64_t* x_stride
   int es;
   const int rc = ps::build(dtype, x, x_strides, cos, sin, tab_strides, out, out_strides, B, L, H, D, &p, &es);
   if (rc != PS_OK) return rc;
-  if (p.total_vecs == 0) return PS_OK;
-  const int threads = 256;
-  const int64_t per_block = static_cast<int64_t>(threads) * ps::kVecsPerThread;
-  const int64_t blocks = (p.total_vecs + per_block - 1) / per_block;
-  if (blocks > 0x7fffffffLL) return ps::fail(PS_ERR_UNSUPPORTED, "grid of %lld CTAs", (long long)blocks);
+  if (p.tokens == 0) return PS_OK;
+  // Head chunks: at most kMaxHeads per thread, and enough chunks that the grid
+  // fills the GPU (two CTAs of kThreads per SM slot of 2048 threads) when the
+  // window is short; chunks are balanced so no blockIdx.y row runs a short tail.
+  const int64_t threads_x = static_cast<int64_t>(p.tokens) * p.vph;
+  const int64_t target = static_cast<int64_t>(ps::sm_count()) * 2048;
+  int64_t split = (p.heads + ps::kMaxHeads - 1) / ps::kMaxHeads;
+  const int64_t want = (target + threads_x - 1) / threads_x;
+  if (want > split) split = want < p.heads ? want : p.heads;
+  p.heads_per_block = static_cast<int32_t>((p.heads + split - 1) / split);
+  split = (p.heads + p.heads_per_block - 1) / p.heads_per_block;
+  const int64_t blocks = (threads_x + ps::kThreads - 1) / ps::kThreads;
+  if (blocks > 0x7fffffffLL || split > 65535)
+    return ps::fail(PS_ERR_UNSUPPORTED, "grid of %lld x %lld CTAs", (long long)blocks, (long long)split);
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(split));
+  const int threads = ps::kThreads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (es == 2)
-    ps::rope_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+    ps::rope_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(p);
   else
-    ps::rope_kernel<float><<<static_cast<unsigned>(blocks), threads, 0, s>>>(p);
+    ps::rope_kernel<float><<<grid, threads, 0, s>>>(p);
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "rope launch: %s", cudaGetErrorString(err));
   return PS_OK;

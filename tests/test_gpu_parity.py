@@ -45,6 +45,31 @@ def test_rope_in_place_and_out_argument(golden):
     assert torch.equal(x.cpu(), case["out"])
 
 
+@pytest.mark.parametrize("B,L,H,D,dtype,layout,table_batch", [
+    (1, 34320, 12, 128, torch.bfloat16, "window", 1),   # the 1.3B window, 2 head chunks of 6
+    (1, 1560, 40, 128, torch.bfloat16, "window", 1),    # 14B heads: 5 chunks of 8
+    (2, 300, 3, 128, torch.bfloat16, "bld", 1),         # short: one head per chunk, tables broadcast over B
+    (3, 77, 9, 48, torch.bfloat16, "bhld", 3),          # vph 6 (magic division), per-member tables, 9 = 8 + 1
+    (2, 513, 17, 64, torch.float32, "bld", 2),          # fp32, 17 heads = 3 chunks
+    (1, 5, 1, 8, torch.bfloat16, "bld", 1),             # a single slice per token
+])
+def test_rope_head_chunks_bit_exact(B, L, H, D, dtype, layout, table_batch):
+    """Every head-chunk split of the per-token thread mapping, for several stride orders of
+    [B, L, H] and table batch strides, against the oracle's _rope: bit-exact."""
+    g = torch.Generator().manual_seed(B * 1000 + H)
+    if layout == "window":   # x is the transposed view of a [B, H, L, D] window
+        x = torch.randn(B, H, L, D, generator=g).to(dtype).transpose(1, 2)
+    elif layout == "bhld":   # [B, L, H, D] view of a [H, B, L, D] storage
+        x = torch.randn(H, B, L, D, generator=g).to(dtype).permute(1, 2, 0, 3)
+    else:
+        x = torch.randn(B, L, H, D, generator=g).to(dtype)
+    cos = torch.randn(table_batch, L, 1, D, generator=g)
+    sin = torch.randn(table_batch, L, 1, D, generator=g)
+    want = oracle.rope(x, cos, sin)
+    got = rope(x.to(DEV), cos.to(DEV), sin.to(DEV))
+    assert torch.equal(got.cpu(), want)
+
+
 def test_rope_empty_input():
     x = torch.empty(1, 0, 2, 128, device=DEV, dtype=torch.bfloat16)
     t = torch.empty(1, 0, 1, 128, device=DEV)
