@@ -781,6 +781,89 @@ def run_processor(args):
     return 0
 
 
+def _event_loop(fn, steps, warmup):
+    """Average device time (us) of ``fn(i)`` over ``steps`` launches after ``warmup``."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    begin.record()
+    for i in range(steps):
+        fn(i)
+    finish.record()
+    torch.cuda.synchronize()
+    return 1000 * begin.elapsed_time(finish) / steps
+
+
+def run_ltx(args):
+    """LTX-2.5 video profile (32 heads x 128, one 17 x 30 latent frame = 510 tokens per chunk;
+    physisserve/models/ltx2.py): ``ps_qk_norm_rope_tables`` over 16 streams' chunks in the ring
+    layout (q, k, v in; rotated q, rotated k and v at each stream's ring rows out) with the
+    reference's explicit per-(token, head) tables, and ``ps_rope_tables`` on a 22-frame K window
+    (the reference layout's window rope).  Two input sets alternate; every launch reads more
+    than L2 holds.  Algorithmic bytes per token: 12*C (activations) + 2*H*w*4 (cos and sin,
+    w = D/2 split or D interleaved)."""
+    from physisserve_b200.ops import qk_norm_rope_tables, rope_tables
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    style = args.ltx_style
+    S, T, H, D = 16, 510, 32, 128
+    C, width = H * D, (D // 2 if style == "split" else D)
+    g = torch.Generator().manual_seed(17)
+
+    def tables(batch, tokens):
+        angle = torch.rand(batch, tokens, H, width, generator=g) * 6.3
+        return angle.cos().to(device), angle.sin().to(device)   # indexed [B, T, H, w]
+
+    sets = []
+    for _ in range(2):
+        q, k, v = (torch.randn(S * T, C, generator=g).bfloat16().to(device) for _ in range(3))
+        sets.append((q, k, v, *tables(S, T)))
+    wq = (torch.rand(C, generator=g) + 0.5).to(device)
+    wk = (torch.rand(C, generator=g) + 0.5).to(device)
+    capacity = 19
+    ring_k = torch.empty(S * capacity * T, C, dtype=torch.bfloat16, device=device)
+    ring_v = torch.empty_like(ring_k)
+    q_out = torch.empty(S * T, C, dtype=torch.bfloat16, device=device)
+    row0 = [s * capacity * T + (s % capacity) * T for s in range(S)]
+
+    def prep(i):
+        q, k, v, cos, sin = sets[i % 2]
+        qk_norm_rope_tables(heads=H, head_dim=D, style=style, batch=S, tokens=T, cos=cos, sin=sin, q=q, k=k, v=v,
+                            q_weight=wq, k_weight=wk, eps=1e-6, q_out=q_out, k_out=ring_k, v_out=ring_v,
+                            kv_row0=row0, heads_per_thread=args.heads_per_thread)
+
+    prep_us = _event_loop(prep, args.steps, args.warmup)
+    prep_bytes = S * T * (12 * C + 2 * H * width * 4)
+    del sets
+
+    W = 22 * T
+    windows = [torch.randn(1, W, C, generator=g).bfloat16().to(device) for _ in range(2)]
+    wtables = [tables(1, W) for _ in range(2)]
+    wout = torch.empty(1, W, C, dtype=torch.bfloat16, device=device)
+
+    def window(i):
+        cos, sin = wtables[i % 2]
+        rope_tables(windows[i % 2].view(1, W, H, D), cos, sin, style, out=wout.view(1, W, H, D))
+
+    window_us = _event_loop(window, args.steps, args.warmup)
+    window_bytes = W * (4 * C + 2 * H * width * 4)
+    peak, src = measured_peak()
+    tokens = S * T
+    achieved = prep_bytes / (prep_us * 1e-6) / 1e9
+    w_achieved = window_bytes / (window_us * 1e-6) / 1e9
+    emit({"impl": "ltx", "metric": "ltx_prep_tokens_per_s", "unit": "tokens/s", "value": tokens / (prep_us * 1e-6),
+          "steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "dtype": "bf16", "data": "synthetic",
+          "config": {"workload": f"LTX-2.5 video, 16 streams x 510 tokens, H=32 D=128, {style} tables, ring layout",
+                     "l2": "two input sets alternate; each launch reads more than L2"},
+          "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                       "bytes_per_launch": prep_bytes, "launch_us": prep_us, "peak_source": src},
+          "window_rope": {"tokens": W, "launch_us": window_us, "achieved": w_achieved, "frac": w_achieved / peak,
+                          "bytes_per_launch": window_bytes}})
+    return 0
+
+
 def run_rope_window(args):
     """ps_rope (the _rope drop-in) on the reference layout's K window at steady state: a
     [1, 12, 34320, 128] bf16 window (22 frames of a 1.3B stream) rotated through its transposed
@@ -932,6 +1015,9 @@ def main(argv=None):
     parser.add_argument("--vstages", type=int, default=0, help="bulk kernel: V stages per CTA (0 = auto)")
     parser.add_argument("--vdepth", type=int, default=0, help="bulk kernel: V stores in flight (0 = auto)")
     parser.add_argument("--cells", type=int, default=0, help="launches per step override (profiling runs)")
+    parser.add_argument("--ltx", action="store_true",
+                        help="time the LTX-2.5 explicit-table prep (ring layout) and window rope")
+    parser.add_argument("--ltx-style", choices=("split", "interleaved"), default="split")
     parser.add_argument("--rope-window", action="store_true",
                         help="time ps_rope on the reference layout's 22-frame K window")
     parser.add_argument("--processor", action="store_true",
@@ -949,6 +1035,8 @@ def main(argv=None):
         return run_processor(args)
     if args.rope_window:
         return run_rope_window(args)
+    if args.ltx:
+        return run_ltx(args)
     if args.impl == "torch":
         return run_torch_gpu(args)
     return run_ours(args)

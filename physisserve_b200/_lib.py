@@ -1,4 +1,5 @@
-"""ctypes binding of ``libphysis_b200.so`` (declared in ``include/physis_b200.h``).
+"""ctypes binding of ``libphysis_b200.so`` (declared in ``include/physis_b200.h`` and
+``include/physis_b200_ltx.h``).
 
 The library is loaded from ``physisserve_b200/lib/`` only.  There is no fallback:
 if the shared library is missing, importing the ops raises, so a GPU host can never
@@ -27,9 +28,12 @@ BF16, F32 = 0, 1
 TABLE_TOKENS, TABLE_AXES = 0, 1
 # ps_kernel
 KERNEL_AUTO, KERNEL_ROWS, KERNEL_BULK = 0, 1, 2
+# ps_rope_style
+ROPE_SPLIT, ROPE_INTERLEAVED = 0, 1
 
 EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
-           "ps_device_timeouts", "ps_rope", "ps_rope_validate")
+           "ps_device_timeouts", "ps_rope", "ps_rope_validate",
+           "ps_table_prep_validate", "ps_qk_norm_rope_tables", "ps_rope_tables", "ps_rope_tables_validate")
 
 
 class PsSeq(ctypes.Structure):
@@ -88,6 +92,40 @@ class PsQkPrepArgs(ctypes.Structure):
     ]
 
 
+class PsTablePrepArgs(ctypes.Structure):
+    """``ps_table_prep_args`` (include/physis_b200_ltx.h)."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("weight_dtype", ctypes.c_int32),
+        ("style", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("tokens", ctypes.c_int32),
+        ("heads_per_thread", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("q_stride", ctypes.c_int64),
+        ("k", ctypes.c_void_p), ("k_stride", ctypes.c_int64),
+        ("v", ctypes.c_void_p), ("v_stride", ctypes.c_int64),
+        ("q_weight", ctypes.c_void_p),
+        ("k_weight", ctypes.c_void_p),
+        ("cos", ctypes.c_void_p),
+        ("sin", ctypes.c_void_p),
+        ("tab_batch_stride", ctypes.c_int64),
+        ("tab_token_stride", ctypes.c_int64),
+        ("tab_head_stride", ctypes.c_int64),
+        ("tab_elems", ctypes.c_int64),
+        ("q_out", ctypes.c_void_p), ("q_out_stride", ctypes.c_int64),
+        ("k_pre", ctypes.c_void_p), ("k_pre_stride", ctypes.c_int64),
+        ("k_out", ctypes.c_void_p), ("k_out_stride", ctypes.c_int64),
+        ("v_out", ctypes.c_void_p), ("v_out_stride", ctypes.c_int64),
+        ("kv_out_rows", ctypes.c_int64),
+        ("kv_row0", ctypes.POINTER(ctypes.c_int64)),
+    ]
+
+
 _LIB = None
 
 
@@ -116,6 +154,16 @@ def load() -> ctypes.CDLL:
     lib.ps_rope.argtypes = [*rope_args, ctypes.c_void_p]
     lib.ps_rope_validate.restype = ctypes.c_int32
     lib.ps_rope_validate.argtypes = rope_args
+    lib.ps_table_prep_validate.restype = ctypes.c_int32
+    lib.ps_table_prep_validate.argtypes = [ctypes.c_void_p]
+    lib.ps_qk_norm_rope_tables.restype = ctypes.c_int32
+    lib.ps_qk_norm_rope_tables.argtypes = [ctypes.c_void_p, ctypes.c_void_p]  # (const ps_table_prep_args*, stream)
+    table_rope_args = [ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, i64p, ctypes.c_void_p, ctypes.c_void_p, i64p,
+                       ctypes.c_void_p, i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]
+    lib.ps_rope_tables.restype = ctypes.c_int32
+    lib.ps_rope_tables.argtypes = [*table_rope_args, ctypes.c_void_p]
+    lib.ps_rope_tables_validate.restype = ctypes.c_int32
+    lib.ps_rope_tables_validate.argtypes = table_rope_args
     version = lib.ps_abi_version()
     if version != ABI_VERSION:
         raise ImportError(f"{LIB_PATH} has ABI version {version}, expected {ABI_VERSION}")

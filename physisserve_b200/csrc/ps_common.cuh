@@ -165,6 +165,18 @@ template <> struct Pairs16<float> {
   __device__ __forceinline__ static f32x2 round(f32x2 v) { return v; }
 };
 
+__device__ __forceinline__ f32x2 f2_swap(f32x2 v) {
+  float a, b;
+  f2_split(v, a, b);
+  return f2_make(b, a);
+}
+
+// RMSNorm's 1 / sqrt(mean(x^2) + eps), each step IEEE-rounded (torch's CPU rsqrt is
+// 1/sqrt).
+__device__ __forceinline__ float rstd_of(float ssq, float c, float eps) {
+  return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssq, c), eps)));
+}
+
 // The even/odd rotation of one element pair exactly as _rope evaluates it
 // (wan.py:61-62): each product and the difference/sum rounded separately in
 // fp32, so no fused multiply-add may form.

@@ -164,11 +164,6 @@ __device__ __forceinline__ Token decode_in(const KParams& p, int s, int g) {
   return t;
 }
 
-__device__ __forceinline__ float rstd_of(float ssq, float c, float eps) {
-  // 1 / sqrt(mean(x^2) + eps), each step IEEE-rounded (torch's CPU rsqrt is 1/sqrt).
-  return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssq, c), eps)));
-}
-
 // Reduces (sum q^2, sum k^2) over the tpr threads of a row group; every thread of the
 // group receives bit-identical sums.  `sync` orders the shared partials.
 template <typename Sync>

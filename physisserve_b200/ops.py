@@ -292,6 +292,158 @@ def qk_norm_rope_kv(
 _KERNELS = {"auto": _lib.KERNEL_AUTO, "rows": _lib.KERNEL_ROWS, "bulk": _lib.KERNEL_BULK}
 
 
+# --------------------------------------------------------------------------------------
+# Explicit per-(token, head) tables: split / interleaved rotation (include/physis_b200_ltx.h)
+# --------------------------------------------------------------------------------------
+_STYLES = {"split": _lib.ROPE_SPLIT, "interleaved": _lib.ROPE_INTERLEAVED}
+
+
+def _style_code(style: str) -> int:
+    try:
+        return _STYLES[style]
+    except KeyError:
+        raise PrepError(f"rope style {style!r} is not 'split' or 'interleaved'") from None
+
+
+def _table_view(t: torch.Tensor, name: str, batch: int, tokens: int, heads: int, width: int, device):
+    """(pointer, (batch, token, head) strides, elements from the pointer to the end of the
+    storage) of a fp32 table view indexed [b or 0, t, h, j] with a unit j stride."""
+    if t.dtype is not torch.float32:
+        raise PrepError(f"{name} must be float32 (the reference's tables are fp32)")
+    if not t.is_cuda or t.device != device:
+        raise PrepError(f"{name} must be a CUDA tensor on {device}")
+    if t.dim() != 4 or t.shape[0] not in (1, batch) or tuple(t.shape[1:]) != (tokens, heads, width):
+        raise PrepError(f"{name} must index as [{batch} or 1, {tokens}, {heads}, {width}], got {tuple(t.shape)}")
+    if t.stride(3) != 1 and width > 1:
+        raise PrepError(f"{name} needs a unit stride on its last dimension")
+    strides = (t.stride(0) if t.shape[0] > 1 else 0, t.stride(1), t.stride(2))
+    elems = t.untyped_storage().nbytes() // 4 - t.storage_offset()
+    return t.data_ptr(), strides, elems
+
+
+def rope_tables(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, style: str,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rotation of a strided ``x`` [B, L, H, D] with explicit tables (``ps_rope_tables``).
+
+    ``cos``/``sin`` index as [B or 1, L, H, D/2] ("split": element i pairs with i + D/2) or
+    [B or 1, L, H, D] ("interleaved": elements 2i, 2i+1 pair), any strides with a unit last
+    stride.  Returns ``torch.empty_like(x)`` filled, or writes ``out``.
+    """
+    code = _style_code(style)
+    if x.dim() != 4:
+        raise PrepError(f"x must be [B, L, H, D], got {tuple(x.shape)}")
+    B, L, H, D = x.shape
+    device = _require_cuda(x)
+    width = D // 2 if code == _lib.ROPE_SPLIT else D
+    cp, cst, _ = _table_view(cos, "cos", B, L, H, width, device)
+    sp, sst, _ = _table_view(sin, "sin", B, L, H, width, device)
+    if cst != sst:
+        raise PrepError("cos and sin must have the same strides")
+    if out is None:
+        out = torch.empty_like(x)
+    elif out.shape != x.shape or out.dtype != x.dtype or out.device != x.device:
+        raise PrepError("out must match x in shape, dtype and device")
+    if x.numel() == 0:
+        return out
+    if x.stride(3) != 1 or out.stride(3) != 1:
+        raise PrepError("x and out need a unit stride on the head dimension")
+    _check(_lib.load().ps_rope_tables(_dtype_code(x), code, ctypes.c_void_p(x.data_ptr()),
+                                      _lib.int64_array(x.stride()[:3]), ctypes.c_void_p(cp), ctypes.c_void_p(sp),
+                                      _lib.int64_array(cst), ctypes.c_void_p(out.data_ptr()),
+                                      _lib.int64_array(out.stride()[:3]), B, L, H, D, _stream(device)))
+    return out
+
+
+def qk_norm_rope_tables(
+    *,
+    heads: int,
+    head_dim: int,
+    style: str,
+    batch: int,
+    tokens: int,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    q: torch.Tensor | None = None,
+    k: torch.Tensor | None = None,
+    v: torch.Tensor | None = None,
+    q_weight: torch.Tensor | None = None,
+    k_weight: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    q_out: torch.Tensor | None = None,
+    k_pre: torch.Tensor | None = None,
+    k_out: torch.Tensor | None = None,
+    v_out: torch.Tensor | None = None,
+    kv_row0: Sequence[int] | None = None,
+    heads_per_thread: int = 0,
+) -> None:
+    """One fused launch of ``ps_qk_norm_rope_tables`` over ``batch`` members of ``tokens`` rows.
+
+    Replaces norm_q/norm_k (ltx2.py:72-73), the pre-RoPE K page (ltx2.py:75) and
+    ``rope(query, own)`` (ltx2.py:76).  q/k/v and the outputs are token-major rows of
+    C = heads*head_dim (row of (b, t) = b*tokens + t); ``cos``/``sin`` index as
+    [batch or 1, tokens, heads, D/2 or D] (see ``rope_tables``).  ``k_out``/``v_out`` rows
+    of member b start at ``kv_row0[b]`` (default b*tokens).  Weights may be bf16 or fp32.
+    """
+    code = _style_code(style)
+    C = heads * head_dim
+    ref = q if q is not None else (k if k is not None else v)
+    if ref is None:
+        raise PrepError("q, k and v are all None")
+    dtype = _dtype_code(ref)
+    device = _require_cuda(q, k, v, q_out, k_pre, k_out, v_out, q_weight, k_weight, cos, sin)
+    for name, t in (("q", q), ("k", k), ("v", v), ("q_out", q_out), ("k_out", k_out), ("v_out", v_out),
+                    ("k_pre", k_pre)):
+        if t is not None and t.dtype is not ref.dtype:
+            raise PrepError(f"{name} is {t.dtype}, expected {ref.dtype}")
+    if batch == 0 or tokens == 0:
+        return
+    wdtype = _lib.BF16
+    weights = [w for w in (q_weight, k_weight) if w is not None]
+    for name, w in (("q_weight", q_weight), ("k_weight", k_weight)):
+        if w is not None and (w.numel() != C or not w.is_contiguous()):
+            raise PrepError(f"{name} must be a contiguous [{C}] vector (RMSNorm over all heads)")
+    if weights:
+        if any(w.dtype is not weights[0].dtype for w in weights):
+            raise PrepError("q_weight and k_weight differ in dtype")
+        wdtype = _dtype_code(weights[0])
+    width = head_dim // 2 if code == _lib.ROPE_SPLIT else head_dim
+    rotates = q is not None or (k is not None and k_out is not None)
+    cp = sp = elems = 0
+    strides = (0, 0, 0)
+    if rotates:
+        if cos is None or sin is None:
+            raise PrepError("cos/sin tables are required for a rotation")
+        cp, strides, elems = _table_view(cos, "cos", batch, tokens, heads, width, device)
+        sp, sstr, selems = _table_view(sin, "sin", batch, tokens, heads, width, device)
+        if sstr != strides:
+            raise PrepError("cos and sin must have the same strides")
+        elems = min(elems, selems)
+    qp, qs, q_rows = _rows(q, C, "q")
+    kp, ks, k_rows = _rows(k, C, "k")
+    vp, vs, v_rows = _rows(v, C, "v")
+    qop, qos, qo_rows = _rows(q_out, C, "q_out")
+    kpp, kps, kp_rows = _rows(k_pre, C, "k_pre")
+    kop, kos, ko_rows = _rows(k_out, C, "k_out")
+    vop, vos, vo_rows = _rows(v_out, C, "v_out")
+    for name, rows, t in (("q", q_rows, q), ("k", k_rows, k), ("v", v_rows, v), ("q_out", qo_rows, q_out),
+                          ("k_pre", kp_rows, k_pre)):
+        if t is not None and rows < batch * tokens:
+            raise PrepError(f"{name} has {rows} rows, the call needs {batch * tokens}")
+    kv_rows = min([r for r, t in ((ko_rows, k_out), (vo_rows, v_out)) if t is not None] or [0])
+    if batch > _lib.MAX_SEQS:
+        raise PrepError(f"batch={batch} exceeds {_lib.MAX_SEQS} members per call")
+    row0 = _lib.int64_array(kv_row0) if kv_row0 is not None else None
+    if row0 is not None and len(row0) != batch:
+        raise PrepError("kv_row0 needs one entry per member")
+    args = _lib.PsTablePrepArgs(
+        dtype, wdtype, code, heads, head_dim, batch, tokens, heads_per_thread, float(eps), 0,
+        qp, qs, kp, ks, vp, vs,
+        None if q_weight is None else q_weight.data_ptr(), None if k_weight is None else k_weight.data_ptr(),
+        cp or None, sp or None, strides[0], strides[1], strides[2], elems,
+        qop, qos, kpp, kps, kop, kos, vop, vos, kv_rows, row0)
+    _check(_lib.load().ps_qk_norm_rope_tables(ctypes.byref(args), _stream(device)))
+
+
 def device_timeouts(reset: bool = True) -> int:
     """Bounded waits of the bulk kernel that ran out on the current device (synchronises)."""
     count = ctypes.c_uint32(0)

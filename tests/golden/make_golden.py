@@ -12,6 +12,7 @@ Everything recorded below is computed by the reference's own code:
 * ``WanDiT._frames_table`` / ``WanDiT._rotary`` (wan.py:241-277), run unbound on a small
   stand-in object that carries the RoPE tables, so the window positions, sink relocation and
   table slicing are the reference's;
+* ``phase_aligned_frames`` of the H3 profile (physisserve/models/h3.py:62-73);
 * ``_Attention.__call__`` (wan.py:102-111) with ``Cache`` / ``BatchCache``
   (kv_cache.py:38-78) over a 24-chunk request, with ``torch.nn.RMSNorm`` as norm_q / norm_k
   (the module diffusers' WanAttention uses) -- intermediates are captured by wrapping the
@@ -227,6 +228,22 @@ def attention_cases(wan_module, WanDiT, Chunks, Cache, BatchCache, history_chunk
             "inputs": inputs, "records": records, "batch": batch}
 
 
+def h3_phase_cases(phase_aligned_frames):
+    """``phase_aligned_frames`` (physisserve/models/h3.py:62-73) over a grid of read-set sizes,
+    query lengths, window starts and sink sizes: args [N, 4], results flattened with offsets."""
+    args, values, offsets = [], [], [0]
+    for sink in (1, 2, 3):
+        for query in (1, 2, 3):
+            for start in range(0, 48):
+                for read in range(0, 24):
+                    frames = phase_aligned_frames(read, query, start, sink)
+                    args.append((read, query, start, sink))
+                    values.extend(frames)
+                    offsets.append(len(values))
+    return {"args": torch.tensor(args, dtype=torch.int32), "values": torch.tensor(values, dtype=torch.int16),
+            "offsets": torch.tensor(offsets, dtype=torch.int64)}
+
+
 def _with_cache(processor, cache):
     processor.cache = cache
     return processor
@@ -235,6 +252,7 @@ def _with_cache(processor, cache):
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--reference", required=True, help="path of the PhysisServe source checkout")
+    parser.add_argument("--only", nargs="*", default=None, help="fixture names to write (default: all)")
     args = parser.parse_args(argv)
     sys.path.insert(0, str(Path(args.reference).resolve()))
     torch.set_num_threads(1)
@@ -243,10 +261,18 @@ def main(argv=None):
     from physisserve.models import wan as wan_module
     from physisserve.models.wan import WanDiT, _rope
 
-    torch.save(rope_cases(_rope), HERE / "rope_cases.pt")
-    torch.save(geometry_cases(Chunks, history_chunks), HERE / "geometry.pt")
-    torch.save(rotary_cases(WanDiT, Chunks, history_chunks), HERE / "rotary_tables.pt")
-    torch.save(attention_cases(wan_module, WanDiT, Chunks, Cache, BatchCache, history_chunks), HERE / "attention.pt")
+    from physisserve.models.h3 import phase_aligned_frames
+
+    fixtures = {
+        "rope_cases": lambda: rope_cases(_rope),
+        "geometry": lambda: geometry_cases(Chunks, history_chunks),
+        "rotary_tables": lambda: rotary_cases(WanDiT, Chunks, history_chunks),
+        "attention": lambda: attention_cases(wan_module, WanDiT, Chunks, Cache, BatchCache, history_chunks),
+        "h3_phase": lambda: h3_phase_cases(phase_aligned_frames),
+    }
+    for name, make in fixtures.items():
+        if args.only is None or name in args.only:
+            torch.save(make(), HERE / f"{name}.pt")
     for path in sorted(HERE.glob("*.pt")):
         print(f"{path.name}: {path.stat().st_size / 1e6:.2f} MB")
     return 0

@@ -11,7 +11,7 @@ import torch
 from physisserve_b200 import _lib
 from physisserve_b200.build import INCLUDE, build
 
-HEADER = INCLUDE / "physis_b200.h"
+HEADERS = sorted(INCLUDE.glob("*.h"))
 
 
 @pytest.fixture(scope="module")
@@ -21,8 +21,10 @@ def lib():
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    return re.findall(r"PS_API\s+[\w\s\*]+?\b(ps_\w+)\s*\(", text)
+    names = []
+    for header in HEADERS:
+        names += re.findall(r"PS_API\s+[\w\s\*]+?\b(ps_\w+)\s*\(", header.read_text())
+    return names
 
 
 def test_every_declared_symbol_is_exported(lib):
