@@ -781,6 +781,116 @@ def run_processor(args):
     return 0
 
 
+def run_ltx_processor(args):
+    """One LTX-2.5 video self-attention block call at steady state (chunk 25: a 22-frame window
+    of sink + 18 recent chunks + the chunk, 510 tokens per frame, 32 heads x 128, split RoPE
+    tables, gated attention), timed for three processors on the GPU:
+
+    * ``torch``     -- ltx2._Attention's algorithm (ltx2.py:66-95) in PyTorch ops: RMSNorm,
+                       pre-RoPE pages, window concat, split rotation of Q and of the whole window
+                       (rotation formula restated; diffusers is not available), SDPA, gate;
+    * ``reference`` -- physisserve_b200.ltx.Attention (same layout, fused kernels);
+    * ``ring``      -- physisserve_b200.ltx.RingAttention (rotated K/V written once at the ring
+                       slot, sink re-rotated, SDPA reads the ring in place).
+    """
+    import torch.nn.functional as F
+    from torch import nn
+
+    from physisserve_b200.ltx import Attention, RingAttention
+    from physisserve_b200.wan import RingCache, window_layout
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    H, D, gh, gw = 32, 128, 17, 30
+    C, hw, r = H * D, gh * gw, D // 2
+    chunk = 25
+    g = torch.Generator().manual_seed(5)
+    attn = nn.Module()
+    attn.heads, attn.head_dim, attn.rope_type = H, D, "split"
+    attn.to_q, attn.to_k, attn.to_v = (nn.Linear(C, C) for _ in range(3))
+    attn.norm_q, attn.norm_k = nn.RMSNorm(C, eps=1e-6), nn.RMSNorm(C, eps=1e-6)
+    attn.to_out = nn.ModuleList([nn.Linear(C, C), nn.Identity()])
+    attn.to_gate_logits = nn.Linear(C, H)
+    attn = attn.to(device, torch.bfloat16).eval()
+    hidden = torch.randn(1, hw, C, generator=g).bfloat16().to(device)
+    pos = window_layout(chunk)
+    freq = torch.rand(H, r, generator=g, dtype=torch.float64)
+
+    def tables(first_frame, frames):
+        p = torch.arange(first_frame, first_frame + frames, dtype=torch.float64).repeat_interleave(hw)
+        angle = p[None, :, None] * freq[:, None, :]                        # [H, tokens, r]
+        return angle.cos().float()[None].to(device), angle.sin().float()[None].to(device)
+
+    own = tables(pos.frame_offset, 1)
+    window = tables(pos.sink_position, pos.frame_offset + 1 - pos.sink_position)
+    history = [0, *range(chunk - 18, chunk)]
+    pages = [tuple(torch.randn(1, 1, (3 if c == 0 else 1) * hw, C, generator=g).bfloat16().to(device)
+                   for _ in range(2)) for c in history]
+
+    class Cache:
+        def __init__(self, hist):
+            self.history, self.page = hist, None
+
+        def __call__(self, key, value):
+            self.page = (key, value)
+            parts = [*self.history, (key, value)]
+            return tuple(torch.cat([p[i] for p in parts], dim=2) for i in (0, 1))
+
+    def split_rope(x, freqs):
+        cos, sin = freqs                                                    # [1, H, T, r]
+        b, t, _ = x.shape
+        first, second = x.view(b, t, H, D).float().transpose(1, 2).chunk(2, dim=-1)
+        out = torch.cat((first * cos - second * sin, second * cos + first * sin), dim=-1)
+        return out.transpose(1, 2).reshape(b, t, C).to(x.dtype)
+
+    def torch_processor():
+        gate_logits = attn.to_gate_logits(hidden)
+        query = attn.norm_q(attn.to_q(hidden))
+        key = attn.norm_k(attn.to_k(hidden))
+        value = attn.to_v(hidden)
+        key, value = Cache(pages)(key.unsqueeze(1), value.unsqueeze(1))
+        query = split_rope(query, own)
+        key = split_rope(key.squeeze(1), window)
+        value = value.squeeze(1)
+
+        def heads(x):
+            return x.view(1, x.shape[1], H, D).transpose(1, 2)
+
+        out = F.scaled_dot_product_attention(heads(query), heads(key), heads(value))
+        out = out.transpose(1, 2).reshape(1, hw, -1)
+        out = (out.view(1, hw, H, D) * (2.0 * torch.sigmoid(gate_logits)).unsqueeze(-1)).reshape(1, hw, -1)
+        return attn.to_out[1](attn.to_out[0](out))
+
+    drop_in = Attention()
+
+    def reference_processor():
+        drop_in.cache, drop_in.rotary = Cache(pages), (own, window)
+        return drop_in(attn, hidden)
+
+    ring = RingAttention()
+    ring.cache = RingCache(heads=H, head_dim=D, grid_h=gh, grid_w=gw, device=device)
+    ring.cache.k.normal_()
+    ring.cache.v.normal_()
+    ring.cache.sink_k.normal_()
+    ring.rotary = (own, window, pos)
+
+    def ring_processor():
+        ring.cache.sink_at = [pos.sink_position - 1]  # the sink moved by one frame since the last chunk
+        return ring(attn, hidden)
+
+    results = {}
+    with torch.inference_mode():
+        for name, fn in (("torch", torch_processor), ("reference", reference_processor), ("ring", ring_processor)):
+            results[name] = _event_loop(lambda i: fn(), args.steps, args.warmup) / 1000
+    emit({"impl": "processor", "metric": "block_call_ms", "unit": "ms", "higher_is_better": False,
+          "value": results["ring"], "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+          "config": {"workload": "LTX-2.5 video self-attention block call, chunk 25 (22-frame window), split RoPE",
+                     "tokens": hw, "window_tokens": 22 * hw, "heads": H, "head_dim": D},
+          "ms_per_call": results, "speedup_vs_torch": {k: results["torch"] / v for k, v in results.items()},
+          "gpu": torch.cuda.get_device_name(device)})
+    return 0
+
+
 def _event_loop(fn, steps, warmup):
     """Average device time (us) of ``fn(i)`` over ``steps`` launches after ``warmup``."""
     for i in range(warmup):
@@ -1032,7 +1142,7 @@ def main(argv=None):
     if args.pipeline:
         return run_pipeline(args)
     if args.processor:
-        return run_processor(args)
+        return run_ltx_processor(args) if args.ltx else run_processor(args)
     if args.rope_window:
         return run_rope_window(args)
     if args.ltx:
