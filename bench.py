@@ -117,6 +117,7 @@ class Workload:
         # Algorithmic HBM bytes: read q, k, v and write q', k'-slot, v-slot (bf16): 12*C per token.
         self.bytes_per_token = 12 * C
         self.bytes_per_launch = self.bytes_per_token * self.tokens_per_launch
+        self._chunk_plans = None
 
     def seqs(self, step):
         from physisserve_b200.ops import Seq
@@ -129,30 +130,35 @@ class Workload:
         return out
 
     def run_step(self, step):
-        """Launch one step's kernels on the current stream; returns the number of launches."""
-        from physisserve_b200.ops import Seq, qk_norm_rope_kv
+        """Launch one step's kernels on the current stream; returns the number of launches.
+
+        Launches go through ``ops.PrepPlan``: the step's call is validated and packed once and
+        each launch swaps in its activations (and the block's norm weights), as a serving loop
+        over 30 blocks x 4 denoising steps would."""
+        from physisserve_b200.ops import PrepPlan, Seq
 
         first = step * self.launches_per_step
+        common = dict(heads=self.heads, head_dim=self.head_dim, cos=self.cos, sin=self.sin, eps=1e-6,
+                      q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v, **self.tiling)
         if self.name == "cfg2":
-            for chunk in range(18):
+            if self._chunk_plans is None:
+                q, k, v = self.inputs[0]
+                self._chunk_plans = [
+                    PrepPlan(seqs=[Seq(0, self.hw, self.gh, self.gw, 3 + chunk, 0, 0, self.capacity,
+                                       (3 + chunk) % self.capacity)],
+                             q=q, k=k, v=v, q_weight=self.wq[0], k_weight=self.wk[0], **common)
+                    for chunk in range(18)]
+            for chunk, plan in enumerate(self._chunk_plans):
                 q, k, v = self.inputs[(first + chunk) % len(self.inputs)]
-                offset = 3 + chunk
-                qk_norm_rope_kv(heads=self.heads, head_dim=self.head_dim,
-                                seqs=[Seq(0, self.hw, self.gh, self.gw, offset, 0, 0, self.capacity,
-                                          offset % self.capacity)],
-                                cos=self.cos, sin=self.sin, q=q, k=k, v=v, q_weight=self.wq[0], k_weight=self.wk[0],
-                                eps=1e-6, q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v, **self.tiling)
+                plan.launch(q=q, k=k, v=v)
             return 18
-        seqs = self.seqs(step)
-        n = 0
+        q, k, v = self.inputs[first % len(self.inputs)]
+        plan = PrepPlan(seqs=self.seqs(step), q=q, k=k, v=v, q_weight=self.wq[0], k_weight=self.wk[0], **common)
         for cell in range(self.launches_per_step):
             q, k, v = self.inputs[(first + cell) % len(self.inputs)]
             block = cell % self.n_blocks
-            qk_norm_rope_kv(heads=self.heads, head_dim=self.head_dim, seqs=seqs, cos=self.cos, sin=self.sin, q=q, k=k,
-                            v=v, q_weight=self.wq[block], k_weight=self.wk[block], eps=1e-6, q_out=self.q_out,
-                            k_out=self.ring_k, v_out=self.ring_v, **self.tiling)
-            n += 1
-        return n
+            plan.launch(q=q, k=k, v=v, q_weight=self.wq[block], k_weight=self.wk[block])
+        return self.launches_per_step
 
 
 # --------------------------------------------------------------------------------------

@@ -178,7 +178,7 @@ def _current_stream(device_index: int) -> int:
         return torch.cuda.current_stream(device_index).cuda_stream
 
 
-def qk_norm_rope_kv(
+def _prepare(
     *,
     heads: int,
     head_dim: int,
@@ -206,18 +206,9 @@ def qk_norm_rope_kv(
     release: int = 0,
     vstages: int = 0,
     vdepth: int = 0,
-) -> None:
-    """One fused launch (per ``PS_MAX_SEQS`` sequences) of ``ps_qk_norm_rope_kv``.
-
-    Replaces norm_q/norm_k (wan.py:104-105), the K/V write of ``Cache`` (kv_cache.py:51-56)
-    and ``_rope`` of Q and of the chunk's K (wan.py:108-109).  ``table_mode`` is "axes"
-    (``cos``/``sin`` are the [max_len, D] per-axis tables, positions decoded from each
-    sequence's grid and frame offset) or "tokens" (``cos``/``sin`` are per-token rows,
-    [rows, D] or the reference's [B, L, 1, D] tables, read at ``table_row + l``).
-    ``kernel`` is "auto", "bulk" (persistent cp.async.bulk pipeline) or "rows"; the tiling
-    knobs (``heads_per_thread`` for rows; ``row_threads``, ``stages``, ``groups``,
-    ``ctas_per_sm``, ``release``, ``vstages``, ``vdepth`` for bulk) default to the library's choice.
-    """
+) -> tuple:
+    """Validate a ``qk_norm_rope_kv`` call and pack its ``ps_qk_prep_args`` (one buffer per
+    ``PS_MAX_SEQS`` sequences); returns (device index, [(args, seq buffer)], tensor signatures)."""
     C = heads * head_dim
     ref = q if q is not None else (k if k is not None else v)
     if ref is None:
@@ -269,11 +260,10 @@ def qk_norm_rope_kv(
     if kern is None:
         raise PrepError(f"kernel {kernel!r} is not 'auto', 'bulk' or 'rows'")
 
-    lib = _lib.load()
-    stream = _current_stream(device_index)
     qw = 0 if q_weight is None else q_weight.data_ptr()
     kw = 0 if k_weight is None else k_weight.data_ptr()
     seqs = list(seqs)
+    parts = []
     for begin in range(0, max(1, len(seqs)), _lib.MAX_SEQS):
         part = seqs[begin:begin + _lib.MAX_SEQS]
         seq_buf = ctypes.create_string_buffer(_SEQ.size * max(1, len(part)))
@@ -286,7 +276,75 @@ def qk_norm_rope_kv(
                         in_rows, qp or 0, qs, kp or 0, ks, vp or 0, vs, qw, kw, cos.data_ptr(), sin.data_ptr(),
                         table_rows, qop or 0, qos, kop or 0, kos, vop or 0, vos, kv_rows, kpp or 0, kps,
                         ctypes.addressof(seq_buf))
+        parts.append((args, seq_buf))
+    signatures = {name: _signature(t) for name, t in (("q", q), ("k", k), ("v", v), ("q_weight", q_weight),
+                                                      ("k_weight", k_weight))}
+    return device_index, parts, signatures
+
+
+def _signature(t: torch.Tensor | None):
+    return None if t is None else (t.shape, t.stride(), t.dtype, t.device)
+
+
+def qk_norm_rope_kv(**kwargs) -> None:
+    """One fused launch (per ``PS_MAX_SEQS`` sequences) of ``ps_qk_norm_rope_kv``.
+
+    Replaces norm_q/norm_k (wan.py:104-105), the K/V write of ``Cache`` (kv_cache.py:51-56)
+    and ``_rope`` of Q and of the chunk's K (wan.py:108-109).  Keyword arguments:
+    ``heads``, ``head_dim``, ``seqs`` (``Seq`` list), ``cos``/``sin``, ``q``/``k``/``v``,
+    ``q_weight``/``k_weight``, ``eps``, ``q_out``/``k_out``/``v_out``/``k_pre``,
+    ``table_mode`` -- "axes" (``cos``/``sin`` are the [max_len, D] per-axis tables, positions
+    decoded from each sequence's grid and frame offset) or "tokens" (``cos``/``sin`` are
+    per-token rows, [rows, D] or the reference's [B, L, 1, D] tables, read at
+    ``table_row + l``) -- ``axis_split``, and the tiling knobs ``kernel`` ("auto", "bulk" =
+    persistent cp.async.bulk pipeline, "rows"), ``heads_per_thread`` (rows), ``row_threads``,
+    ``stages``, ``groups``, ``ctas_per_sm``, ``release``, ``vstages``, ``vdepth`` (bulk), all
+    defaulting to the library's choice.
+    """
+    device_index, parts, _ = _prepare(**kwargs)
+    lib = _lib.load()
+    stream = _current_stream(device_index)
+    for args, _seq_buf in parts:
         _check(lib.ps_qk_norm_rope_kv(args, stream))
+
+
+# Byte offsets of the pointer fields a plan swaps between launches.
+_FIELD_OFFSETS = {
+    "q": struct.calcsize("=8if9iq"),
+    "k": struct.calcsize("=8if9iq" + "Qq"),
+    "v": struct.calcsize("=8if9iq" + "Qq" * 2),
+    "q_weight": struct.calcsize("=8if9iq" + "Qq" * 3),
+    "k_weight": struct.calcsize("=8if9iq" + "Qq" * 3 + "Q"),
+}
+
+
+class PrepPlan:
+    """A ``qk_norm_rope_kv`` call validated and packed once, launched many times.
+
+    The per-block loop of a serving step (30 blocks x 4 denoising steps of the same streams)
+    repeats one call shape with new activations and per-block norm weights.  ``launch`` swaps
+    the q/k/v/weight pointers into the packed ``ps_qk_prep_args`` and calls the library; each
+    swapped tensor must have the planned shape, strides, dtype and device (checked), and the
+    library re-validates every launch on the host.  Sequences, tables and outputs are fixed.
+    """
+
+    def __init__(self, **kwargs):
+        self.device_index, self.parts, self.signatures = _prepare(**kwargs)
+        self._lib = _lib.load()
+
+    def launch(self, **tensors) -> None:
+        for name, t in tensors.items():
+            want = self.signatures.get(name, False)
+            if want is False:
+                raise PrepError(f"{name} cannot be swapped in a plan (only q, k, v, q_weight, k_weight)")
+            if want is None or t is None or (t.shape, t.stride(), t.dtype, t.device) != want:
+                raise PrepError(f"{name} must match the planned tensor (shape, strides, dtype, device)")
+            ptr = t.data_ptr()
+            for args, _seq_buf in self.parts:
+                struct.pack_into("=Q", args, _FIELD_OFFSETS[name], ptr)
+        stream = _current_stream(self.device_index)
+        for args, _seq_buf in self.parts:
+            _check(self._lib.ps_qk_norm_rope_kv(args, stream))
 
 
 _KERNELS = {"auto": _lib.KERNEL_AUTO, "rows": _lib.KERNEL_ROWS, "bulk": _lib.KERNEL_BULK}

@@ -655,6 +655,47 @@ def test_fp32_wide_rows(kernel):
         assert torch.equal(ring_v[b, slot * L:(slot + 1) * L], v[b])
 
 
+@pytest.mark.parametrize("kernel", ["rows", "bulk"])
+def test_prep_plan_matches_direct_calls(kernel):
+    """PrepPlan (validate once, swap activations and norm weights per launch) writes exactly
+    what a direct qk_norm_rope_kv call with the same tensors writes."""
+    H, D, gh, gw, capacity = 40 if kernel == "bulk" else 12, 128, 6, 10, 4
+    C, L, B = H * D, gh * gw, 3
+    cos, sin = oracle.rope_tables(D, 64)
+    split = oracle.axis_dims(D)
+    rows = capacity * L
+    seqs = [Seq(b * L, L, gh, gw, frame_offset=5 + b, ring_row=b * rows, ring_frames=capacity,
+                ring_slot0=(5 + b) % capacity) for b in range(B)]
+    inputs = [tuple(randn((B * L, C), seed=40 + 3 * i + j).to(DEV) for j in range(3)) for i in range(2)]
+    weights = [(norm_weight(C, 50 + i).to(DEV), norm_weight(C, 60 + i).to(DEV)) for i in range(2)]
+    dcos, dsin = cos.to(DEV), sin.to(DEV)
+
+    def outputs():
+        return (torch.zeros(B * L, C, device=DEV, dtype=torch.bfloat16),
+                torch.zeros(B * rows, C, device=DEV, dtype=torch.bfloat16),
+                torch.zeros(B * rows, C, device=DEV, dtype=torch.bfloat16))
+
+    planned, direct = outputs(), outputs()
+    plan = ops.PrepPlan(heads=H, head_dim=D, seqs=seqs, cos=dcos, sin=dsin, q=inputs[0][0], k=inputs[0][1],
+                        v=inputs[0][2], q_weight=weights[0][0], k_weight=weights[0][1], eps=EPS, q_out=planned[0],
+                        k_out=planned[1], v_out=planned[2], axis_split=split, kernel=kernel)
+    for i in (1, 0, 1):
+        q, k, v = inputs[i]
+        plan.launch(q=q, k=k, v=v, q_weight=weights[i][0], k_weight=weights[i][1])
+        qk_norm_rope_kv(heads=H, head_dim=D, seqs=seqs, cos=dcos, sin=dsin, q=q, k=k, v=v, q_weight=weights[i][0],
+                        k_weight=weights[i][1], eps=EPS, q_out=direct[0], k_out=direct[1], v_out=direct[2],
+                        axis_split=split, kernel=kernel)
+        torch.cuda.synchronize()
+        for a, b in zip(planned, direct):
+            assert torch.equal(a, b)
+    with pytest.raises(ops.PrepError):
+        plan.launch(q=inputs[0][0][:-1])                       # other shape
+    with pytest.raises(ops.PrepError):
+        plan.launch(q=inputs[0][0].float())                    # other dtype
+    with pytest.raises(ops.PrepError):
+        plan.launch(q_out=planned[0])                          # outputs are fixed in a plan
+
+
 def test_no_bounded_wait_ran_out():
     """After every kernel above, the bulk kernel's bounded mbarrier waits never expired."""
     assert ops.device_timeouts(reset=True) == 0
