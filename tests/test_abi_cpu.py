@@ -195,6 +195,16 @@ def test_packed_arguments_match_the_header_layout():
     assert ops._SEQ.pack(7, 1560, 30, 52, 9, 11, 13, 12, 5) == bytes(seq)
 
 
+def test_plan_pointer_offsets_match_header():
+    """PrepPlan patches q/k/v/q_weight/k_weight into packed ps_qk_prep_args at fixed byte
+    offsets; they must be the header's field offsets."""
+    from physisserve_b200 import ops
+
+    A = _lib.PsQkPrepArgs
+    assert ops._FIELD_OFFSETS == {"q": A.q.offset, "k": A.k.offset, "v": A.v.offset,
+                                  "q_weight": A.q_weight.offset, "k_weight": A.k_weight.offset}
+
+
 @pytest.mark.parametrize("shape,strides,rows,row_stride", [
     ((12480, 5120), (5120, 1), 12480, 5120),
     ((8, 1560, 5120), (1560 * 5120, 5120, 1), 12480, 5120),
