@@ -9,6 +9,7 @@ allocate only the outputs the reference also allocates (``torch.empty_like`` in
 from __future__ import annotations
 
 import ctypes
+import inspect
 import struct
 from dataclasses import dataclass
 from typing import Sequence
@@ -306,6 +307,9 @@ def qk_norm_rope_kv(**kwargs) -> None:
     stream = _current_stream(device_index)
     for args, _seq_buf in parts:
         _check(lib.ps_qk_norm_rope_kv(args, stream))
+
+
+qk_norm_rope_kv.__signature__ = inspect.signature(_prepare).replace(return_annotation=None)
 
 
 # Byte offsets of the pointer fields a plan swaps between launches.
