@@ -117,10 +117,17 @@ def _check_norm(got, want, what):
 @pytest.mark.parametrize("style", ["split", "interleaved"])
 @pytest.mark.parametrize("dtype,wdtype", [(torch.bfloat16, torch.bfloat16), (torch.bfloat16, torch.float32),
                                           (torch.float32, torch.float32)])
-@pytest.mark.parametrize("hpt", [0, 1])
-def test_table_prep_fused(style, dtype, wdtype, hpt):
-    B, T, H, D = 2, 300, 8, 64
+@pytest.mark.parametrize("hpt", [0, 1, 2])
+@pytest.mark.parametrize("B,T,H,D", [
+    (2, 300, 8, 64),     # row groups of 4..64 threads (shuffle-only and two-warp reductions)
+    (2, 64, 32, 128),    # the LTX-2 head layout: row groups of 128..1024 threads -> multi-warp reduction
+])
+def test_table_prep_fused(style, dtype, wdtype, hpt, B, T, H, D):
     C = H * D
+    E = 8 if dtype == torch.bfloat16 else 4          # elements per 16-byte slice
+    slices = D // (2 * E) if style == "split" else D // E
+    if hpt and slices * H // hpt > 512:
+        pytest.skip("row group above 512 threads is rejected by the library (checked in the CPU tests)")
     q, k, v = (randn((B * T, C), seed=s, dtype=dtype) for s in (11, 12, 13))
     wq, wk = norm_weight(C, 14, wdtype), norm_weight(C, 15, wdtype)
     cos, sin = ref_tables(style, B, T, H, D, seed=16)
