@@ -61,12 +61,15 @@ WORKLOADS = {
 class Workload:
     """Device buffers and launch list of one rank's share of a workload."""
 
-    def __init__(self, name, rank, world, device, seed=1234, ring_frames=None, heads_per_thread=0, **tiling):
+    def __init__(self, name, rank, world, device, seed=1234, ring_frames=None, heads_per_thread=0, streams=None,
+                 **tiling):
         from physisserve_b200.wan import wan_rope_tables
 
         spec = dict(WORKLOADS[name])
         if ring_frames:
             spec["capacity"] = ring_frames
+        if streams:
+            spec["streams"] = streams
         self.tiling = dict(heads_per_thread=heads_per_thread, **tiling)
         self.name, self.spec, self.device = name, spec, device
         self.heads, self.head_dim = spec["heads"], spec["head_dim"]
@@ -388,7 +391,7 @@ def run_ours(args):
     from physisserve_b200 import _lib
 
     _lib.load()
-    work = Workload(args.workload, rank, world, device, ring_frames=args.ring_frames,
+    work = Workload(args.workload, rank, world, device, ring_frames=args.ring_frames, streams=args.streams,
                     heads_per_thread=args.heads_per_thread, kernel=args.kernel, stages=args.stages,
                     groups=args.groups, ctas_per_sm=args.ctas_per_sm, row_threads=args.row_threads,
                     release=args.release, vstages=args.vstages, vdepth=args.vdepth)
@@ -1115,6 +1118,8 @@ def main(argv=None):
                              "torch: the reference algorithm as PyTorch ops on the GPU")
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3")
     parser.add_argument("--graph", action="store_true", help="replay each step from a captured CUDA graph")
+    parser.add_argument("--streams", type=int, default=None,
+                        help="override the workload's stream count (e.g. cfg5 --streams 8 = one rank's share at N=8)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--e2e-steps", type=int, default=20)
