@@ -18,55 +18,11 @@ void clear_error();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// A 16-byte vector of activations: 8 bf16 or 4 fp32 elements, converted to and
-// from fp32 registers.  bf16 -> fp32 is exact; fp32 -> bf16 rounds to nearest
-// even (the rounding of a PyTorch bf16 store).
+// A 16-byte vector of activations: 8 bf16 or 4 fp32 elements.  Conversions to and
+// from fp32 pairs live in Pairs16 below.
 template <typename T> struct Vec16;
-
-template <> struct Vec16<__nv_bfloat16> {
-  static constexpr int kElems = 8;
-  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[2 * i] = __uint_as_float(w[i] << 16);
-      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
-  }
-  __device__ __forceinline__ static uint4 pack(const float* f) {
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-      w[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    return make_uint4(w[0], w[1], w[2], w[3]);
-  }
-  // Rounds two fp32 values to the element type and back (exact widening).  The
-  // paired conversion (cvt.rn.bf16x2.f32) keeps the rounding off the XU pipe that a
-  // per-element float->bf16 conversion would saturate.
-  __device__ __forceinline__ static void round_pair(float& a, float& b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    const uint32_t u = *reinterpret_cast<uint32_t*>(&h);
-    a = __uint_as_float(u << 16);
-    b = __uint_as_float(u & 0xffff0000u);
-  }
-};
-
-template <> struct Vec16<float> {
-  static constexpr int kElems = 4;
-  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
-    f[0] = __uint_as_float(u.x);
-    f[1] = __uint_as_float(u.y);
-    f[2] = __uint_as_float(u.z);
-    f[3] = __uint_as_float(u.w);
-  }
-  __device__ __forceinline__ static uint4 pack(const float* f) {
-    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
-                      __float_as_uint(f[3]));
-  }
-  __device__ __forceinline__ static void round_pair(float&, float&) {}
-};
+template <> struct Vec16<__nv_bfloat16> { static constexpr int kElems = 8; };
+template <> struct Vec16<float> { static constexpr int kElems = 4; };
 
 // Read-once activation loads: read-only path without L1 allocation, so the
 // streamed rows do not displace the RoPE tables / weights held in L1.  Volatile
@@ -178,17 +134,9 @@ __device__ __forceinline__ float rstd_of(float ssq, float c, float eps) {
 }
 
 // The even/odd rotation of one element pair exactly as _rope evaluates it
-// (wan.py:61-62): each product and the difference/sum rounded separately in
-// fp32, so no fused multiply-add may form.
-__device__ __forceinline__ void rotate_pair(float e, float o, float cos_e, float cos_o, float sin_e,
-                                            float sin_o, float& out_e, float& out_o) {
-  out_e = __fsub_rn(__fmul_rn(e, cos_e), __fmul_rn(o, sin_o));
-  out_o = __fadd_rn(__fmul_rn(e, sin_e), __fmul_rn(o, cos_o));
-}
-
-// The same rotation on packed operands: pair (e, o) with cos pair (cos[2i], cos[2i+1])
-// and sin pair (sin[2i], sin[2i+1]); two packed products and two scalar adds, the
-// three roundings of _rope per output.
+// (wan.py:61-62): pair (e, o) with cos pair (cos[2i], cos[2i+1]) and sin pair
+// (sin[2i], sin[2i+1]); two packed products and a scalar difference and sum, each
+// rounded separately in fp32 (no fused multiply-add may form).
 __device__ __forceinline__ void rotate_f2(f32x2 x, f32x2 c, f32x2 sn, float& lo, float& hi) {
   float m1e, m1o, m2e, m2o;
   f2_split(f2_mul(x, c), m1e, m1o);   // (e*cos[2i], o*cos[2i+1])
