@@ -148,7 +148,7 @@ extern "C" int32_t ps_rope_validate(int32_t dtype, const void* x, const int64_t*
                                     const float* sin, const int64_t* tab_strides, void* out,
                                     const int64_t* out_strides, int64_t B, int64_t L, int64_t H, int64_t D) {
   ps::RopeParams p;
-  int es;
+  int es = 0;
   return ps::build(dtype, x, x_strides, cos, sin, tab_strides, out, out_strides, B, L, H, D, &p, &es);
 }
 
@@ -156,7 +156,7 @@ extern "C" int32_t ps_rope(int32_t dtype, const void* x, const int64_t* x_stride
                            const int64_t* tab_strides, void* out, const int64_t* out_strides, int64_t B, int64_t L,
                            int64_t H, int64_t D, void* stream) {
   ps::RopeParams p;
-  int es;
+  int es = 0;
   const int rc = ps::build(dtype, x, x_strides, cos, sin, tab_strides, out, out_strides, B, L, H, D, &p, &es);
   if (rc != PS_OK) return rc;
   if (p.tokens == 0) return PS_OK;

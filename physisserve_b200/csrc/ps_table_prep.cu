@@ -582,7 +582,7 @@ extern "C" int32_t ps_rope_tables_validate(int32_t dtype, int32_t style, const v
                                            const float* cos, const float* sin, const int64_t* tab_strides, void* out,
                                            const int64_t* out_strides, int64_t B, int64_t L, int64_t H, int64_t D) {
   ps::RtParams p;
-  int es;
+  int es = 0;
   return ps::build_rope_tables(dtype, style, x, x_strides, cos, sin, tab_strides, out, out_strides, B, L, H, D, &p, &es);
 }
 
@@ -591,7 +591,7 @@ extern "C" int32_t ps_rope_tables(int32_t dtype, int32_t style, const void* x, c
                                   const int64_t* out_strides, int64_t B, int64_t L, int64_t H, int64_t D,
                                   void* stream) {
   ps::RtParams p;
-  int es;
+  int es = 0;
   const int rc = ps::build_rope_tables(dtype, style, x, x_strides, cos, sin, tab_strides, out, out_strides, B, L, H, D,
                                        &p, &es);
   if (rc != PS_OK) return rc;
