@@ -42,7 +42,7 @@ def _table_views(tables, style: str, heads: int):
     return cos.unflatten(-1, (heads, -1)), sin.unflatten(-1, (heads, -1))
 
 
-def _heads_of(tables, style: str, x: torch.Tensor) -> int:
+def _heads_of(tables, style: str) -> int:
     if style == "split":
         return tables[0].shape[1]
     return 1  # the interleaved pairs never cross a head boundary: any head count rotates alike
@@ -51,7 +51,7 @@ def _heads_of(tables, style: str, x: torch.Tensor) -> int:
 def _rotate(x: torch.Tensor, tables, style: str, heads: int | None = None) -> torch.Tensor:
     if x.dim() != 3:
         raise PrepError(f"x must be [B, tokens, heads*D], got {tuple(x.shape)}")
-    H = heads or _heads_of(tables, style, x)
+    H = heads or _heads_of(tables, style)
     B, T, C = x.shape
     if C % H:
         raise PrepError(f"inner dim {C} is not a multiple of {H} heads")
