@@ -245,3 +245,45 @@ def test_ltx_processors_over_a_request(style):
             assert float((out_ours - out_ref).abs().max()) <= PROC_REL * scale, f"chunk {chunk}: drop-in"
             assert float((out_ring - out_ours).abs().max()) <= PROC_REL * scale, f"chunk {chunk}: ring"
     check_bf16_close(pages_ours[5][0].cpu(), pages_ref[5][0].cpu(), "pre-RoPE K page")
+
+
+@pytest.mark.parametrize("style", ["split", "interleaved"])
+def test_ltx_block_batch_equals_serial(style):
+    """LTX2DiT.block_batch (ltx2.py:352-372): members with equal history lengths packed along
+    the batch, their tables stacked (_batch_rotary) and a BatchCache -- the drop-in's packed
+    call equals its serial calls, matches the oracle processor on the packed call, and each
+    member's retained page is its own."""
+    H, D, hw = 4, 32, 6
+    C = H * D
+    chunks = (20, 23)                      # both read the sink + 18 recent pages
+    attn = _StubAttention(C, H, style, gated=False, seed=11).to(DEV, torch.bfloat16)
+    members = []
+    for m, chunk in enumerate(chunks):
+        history = wan_oracle.history_chunks(chunk)
+        pages = [tuple(randn((1, 1, _frames(c) * hw, C), seed=5000 + 100 * m + 2 * c + i).to(DEV) for i in range(2))
+                 for c in history]
+        win_pos, own_pos = _window_positions(chunk, hw)
+        own = _cuda(ref_tables(style, 1, hw, H, D, seed=9, positions=own_pos))
+        window = _cuda(ref_tables(style, 1, len(win_pos), H, D, seed=9, positions=win_pos))
+        members.append((randn((1, hw, C), seed=6000 + m).to(DEV), pages, own, window))
+    packed_own = tuple(torch.cat([mb[2][i] for mb in members]) for i in range(2))
+    packed_window = tuple(torch.cat([mb[3][i] for mb in members]) for i in range(2))
+    hidden = torch.cat([mb[0] for mb in members])
+    with torch.no_grad():
+        ours, ref = ltx.Attention(), oracle.Attention()
+        caches_ours = [wan_oracle.Cache(mb[1]) for mb in members]
+        caches_ref = [wan_oracle.Cache(mb[1]) for mb in members]
+        ours.cache, ours.rotary = wan_oracle.BatchCache(caches_ours, 1), (packed_own, packed_window)
+        ref.cache, ref.rotary = wan_oracle.BatchCache(caches_ref, 1), (packed_own, packed_window)
+        packed = ours(attn, hidden)
+        packed_ref = ref(attn, hidden)
+        scale = float(packed_ref.abs().max())
+        assert float((packed - packed_ref).abs().max()) <= PROC_REL * scale, "packed drop-in vs oracle"
+        for m, (h, pages, own, window) in enumerate(members):
+            serial = ltx.Attention()
+            serial.cache, serial.rotary = wan_oracle.Cache(pages), (own, window)
+            out = serial(attn, h)
+            assert float((packed[m:m + 1] - out).abs().max()) <= PROC_REL * scale, f"member {m}: packed vs serial"
+            mine, alone = caches_ours[m].page[0], serial.cache.page[0]   # same member, packed vs alone
+            assert mine.shape == alone.shape and mine.data_ptr() != hidden.data_ptr()
+            assert float((mine - alone).abs().max()) <= PROC_REL * float(alone.abs().max()), f"member {m} page"
