@@ -8,6 +8,7 @@ allocate only the outputs the reference also allocates (``torch.empty_like`` in
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import inspect
 import struct
@@ -34,6 +35,12 @@ def _dtype_code(t: torch.Tensor) -> int:
 
 def _stream(device: torch.device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _on_device(index: int):
+    """Make the tensors' device current for the launch (a kernel launched on a stream of
+    another device than the current one fails); free when it already is."""
+    return contextlib.nullcontext() if torch.cuda.current_device() == index else torch.cuda.device(index)
 
 
 def _check(status: int) -> None:
@@ -87,10 +94,11 @@ def rope(x: torch.Tensor, cosine: torch.Tensor, sine: torch.Tensor, out: torch.T
         raise PrepError("x and out need a unit stride on the head dimension")
     tab_batch = 0 if cosine.shape[0] == 1 else cosine.stride(0)
     lib = _lib.load()
-    status = lib.ps_rope(_dtype_code(x), ctypes.c_void_p(x.data_ptr()), _lib.int64_array(x.stride()[:3]),
-                         ctypes.c_void_p(cosine.data_ptr()), ctypes.c_void_p(sine.data_ptr()),
-                         _lib.int64_array((tab_batch, cosine.stride(1))), ctypes.c_void_p(out.data_ptr()),
-                         _lib.int64_array(out.stride()[:3]), B, L, H, D, _stream(device))
+    with _on_device(device.index):
+        status = lib.ps_rope(_dtype_code(x), ctypes.c_void_p(x.data_ptr()), _lib.int64_array(x.stride()[:3]),
+                             ctypes.c_void_p(cosine.data_ptr()), ctypes.c_void_p(sine.data_ptr()),
+                             _lib.int64_array((tab_batch, cosine.stride(1))), ctypes.c_void_p(out.data_ptr()),
+                             _lib.int64_array(out.stride()[:3]), B, L, H, D, _stream(device))
     _check(status)
     return out
 
@@ -304,9 +312,10 @@ def qk_norm_rope_kv(**kwargs) -> None:
     """
     device_index, parts, _ = _prepare(**kwargs)
     lib = _lib.load()
-    stream = _current_stream(device_index)
-    for args, _seq_buf in parts:
-        _check(lib.ps_qk_norm_rope_kv(args, stream))
+    with _on_device(device_index):
+        stream = _current_stream(device_index)
+        for args, _seq_buf in parts:
+            _check(lib.ps_qk_norm_rope_kv(args, stream))
 
 
 qk_norm_rope_kv.__signature__ = inspect.signature(_prepare).replace(return_annotation=None)
@@ -346,9 +355,10 @@ class PrepPlan:
             ptr = t.data_ptr()
             for args, _seq_buf in self.parts:
                 struct.pack_into("=Q", args, _FIELD_OFFSETS[name], ptr)
-        stream = _current_stream(self.device_index)
-        for args, _seq_buf in self.parts:
-            _check(self._lib.ps_qk_norm_rope_kv(args, stream))
+        with _on_device(self.device_index):
+            stream = _current_stream(self.device_index)
+            for args, _seq_buf in self.parts:
+                _check(self._lib.ps_qk_norm_rope_kv(args, stream))
 
 
 _KERNELS = {"auto": _lib.KERNEL_AUTO, "rows": _lib.KERNEL_ROWS, "bulk": _lib.KERNEL_BULK}
@@ -409,10 +419,11 @@ def rope_tables(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, style: st
         return out
     if x.stride(3) != 1 or out.stride(3) != 1:
         raise PrepError("x and out need a unit stride on the head dimension")
-    _check(_lib.load().ps_rope_tables(_dtype_code(x), code, ctypes.c_void_p(x.data_ptr()),
-                                      _lib.int64_array(x.stride()[:3]), ctypes.c_void_p(cp), ctypes.c_void_p(sp),
-                                      _lib.int64_array(cst), ctypes.c_void_p(out.data_ptr()),
-                                      _lib.int64_array(out.stride()[:3]), B, L, H, D, _stream(device)))
+    with _on_device(device.index):
+        _check(_lib.load().ps_rope_tables(_dtype_code(x), code, ctypes.c_void_p(x.data_ptr()),
+                                          _lib.int64_array(x.stride()[:3]), ctypes.c_void_p(cp), ctypes.c_void_p(sp),
+                                          _lib.int64_array(cst), ctypes.c_void_p(out.data_ptr()),
+                                          _lib.int64_array(out.stride()[:3]), B, L, H, D, _stream(device)))
     return out
 
 
@@ -503,7 +514,8 @@ def qk_norm_rope_tables(
         None if q_weight is None else q_weight.data_ptr(), None if k_weight is None else k_weight.data_ptr(),
         cp or None, sp or None, strides[0], strides[1], strides[2], elems,
         qop, qos, kpp, kps, kop, kos, vop, vos, kv_rows, row0)
-    _check(_lib.load().ps_qk_norm_rope_tables(ctypes.byref(args), _stream(device)))
+    with _on_device(device.index):
+        _check(_lib.load().ps_qk_norm_rope_tables(ctypes.byref(args), _stream(device)))
 
 
 def device_timeouts(reset: bool = True) -> int:

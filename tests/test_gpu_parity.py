@@ -696,6 +696,33 @@ def test_prep_plan_matches_direct_calls(kernel):
         plan.launch(q_out=planned[0])                          # outputs are fixed in a plan
 
 
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensors_on_another_device_than_the_current_one():
+    """One process driving two GPUs: the wrappers launch on the tensors' device whatever the
+    current device is, and leave the current device as it was."""
+    dev = "cuda:1"
+    torch.cuda.set_device(0)
+    case_x = randn((1, 24, 2, 128), seed=70)
+    cos, sin = oracle.rope_tables(128, 16)
+    c, s = oracle.frames_table(cos, sin, oracle.axis_dims(128), 3, 5, 3, 4)
+    got = rope(case_x.to(dev), c.to(dev), s.to(dev))
+    assert got.device == torch.device(dev) and torch.cuda.current_device() == 0
+    assert torch.equal(got.cpu(), oracle.rope(case_x, c, s))
+    H, D, gh, gw = 12, 128, 3, 4
+    L, C = gh * gw, H * D
+    q, k, v = (randn((1, L, C), seed=71 + i) for i in range(3))
+    wq, wk = norm_weight(C, 74), norm_weight(C, 75)
+    ring_k = torch.zeros(4 * L, C, device=dev, dtype=torch.bfloat16)
+    ring_v = torch.zeros_like(ring_k)
+    q_out = torch.empty(L, C, device=dev, dtype=torch.bfloat16)
+    qk_norm_rope_kv(heads=H, head_dim=D, seqs=[Seq(0, L, gh, gw, 6, 0, 0, 4, 2)], cos=cos.to(dev), sin=sin.to(dev),
+                    q=q[0].to(dev), k=k[0].to(dev), v=v[0].to(dev), q_weight=wq.to(dev), k_weight=wk.to(dev),
+                    eps=EPS, q_out=q_out, k_out=ring_k, v_out=ring_v)
+    torch.cuda.synchronize(dev)
+    assert torch.cuda.current_device() == 0
+    assert torch.equal(ring_v[2 * L:3 * L].cpu(), v[0])
+
+
 def test_no_bounded_wait_ran_out():
     """After every kernel above, the bulk kernel's bounded mbarrier waits never expired."""
     assert ops.device_timeouts(reset=True) == 0
