@@ -914,6 +914,55 @@ def _event_loop(fn, steps, warmup):
     return 1000 * begin.elapsed_time(finish) / steps
 
 
+class LtxCpuReference:
+    """The LTX-2.5 prep on the host cores (oracle restatement: RMSNorm over C, split or
+    interleaved rotation of Q and K with the chunk's tables, rotated K and V written at the
+    chunk's ring rows), one 510-token stream chunk per step, all host threads."""
+
+    def __init__(self, style, seed=21):
+        from oracle import ltx_prep as oracle
+
+        self.oracle, self.style = oracle, style
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        H, D, T = 32, 128, 510
+        C = H * D
+        self.heads, self.tokens = H, T
+        g = torch.Generator().manual_seed(seed)
+        self.q, self.k, self.v = (torch.randn(1, T, C, generator=g).bfloat16() for _ in range(3))
+        self.weights = ((torch.rand(C, generator=g) + 0.5), (torch.rand(C, generator=g) + 0.5))
+        angle = torch.rand(1, H, T, D // 2, generator=g, dtype=torch.float64) * 6.3
+        if style == "split":
+            self.tables = (angle.cos().float(), angle.sin().float())
+        else:
+            inter = angle.transpose(1, 2).repeat_interleave(2, -1).flatten(-2)
+            self.tables = (inter.cos().float(), inter.sin().float())
+        self.ring_k = torch.zeros(19 * T, C, dtype=torch.bfloat16)
+        self.ring_v = torch.zeros_like(self.ring_k)
+        self.slot = 0
+
+    def step(self):
+        o = self.oracle
+        qn = o.rms_norm(self.q.float(), self.weights[0], 1e-6).bfloat16()
+        kn = o.rms_norm(self.k.float(), self.weights[1], 1e-6).bfloat16()
+        o.rope(qn, self.tables, self.style, self.heads)
+        rows = torch.arange(self.slot * self.tokens, (self.slot + 1) * self.tokens)
+        self.ring_k.index_copy_(0, rows, o.rope(kn, self.tables, self.style, self.heads)[0])
+        self.ring_v.index_copy_(0, rows, self.v[0])
+        self.slot = (self.slot + 1) % 19
+        return self.tokens
+
+    def sample(self, seconds=10.0, min_steps=3):
+        self.step()
+        steps, tokens = 0, 0
+        t0 = time.perf_counter()
+        while steps < min_steps or time.perf_counter() - t0 < seconds:
+            tokens += self.step()
+            steps += 1
+        elapsed = time.perf_counter() - t0
+        return tokens / elapsed, steps, elapsed
+
+
 def run_ltx(args):
     """LTX-2.5 video profile (32 heads x 128, one 17 x 30 latent frame = 510 tokens per chunk;
     physisserve/models/ltx2.py): ``ps_qk_norm_rope_tables`` over 16 streams' chunks in the ring
@@ -971,6 +1020,12 @@ def run_ltx(args):
     peak, src = measured_peak()
     tokens = S * T
     achieved = prep_bytes / (prep_us * 1e-6) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        ref = LtxCpuReference(style)
+        cpu_value, cpu_steps, cpu_s = ref.sample(args.cpu_seconds)
+        cpu = {"value": cpu_value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+               "sample": f"{cpu_steps} stream chunks of {ref.tokens} tokens in {cpu_s:.1f} s", "cpu": cpu_model()}
     w_achieved = window_bytes / (window_us * 1e-6) / 1e9
     emit({"impl": "ltx", "metric": "ltx_prep_tokens_per_s", "unit": "tokens/s", "value": tokens / (prep_us * 1e-6),
           "steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "dtype": "bf16", "data": "synthetic",
@@ -979,7 +1034,8 @@ def run_ltx(args):
           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                        "bytes_per_launch": prep_bytes, "launch_us": prep_us, "peak_source": src},
           "window_rope": {"tokens": W, "launch_us": window_us, "achieved": w_achieved, "frac": w_achieved / peak,
-                          "bytes_per_launch": window_bytes}})
+                          "bytes_per_launch": window_bytes},
+          "cpu_baseline": cpu})
     return 0
 
 
