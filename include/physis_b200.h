@@ -177,6 +177,12 @@ PS_API int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream);
  * current device since the last reset.  Synchronises the device first. */
 PS_API int32_t ps_device_timeouts(uint32_t* count, int32_t reset);
 
+/* Self-test of that bounded wait (no reference counterpart): one CTA waits on an
+ * mbarrier that never completes; the wait gives up after limit_us (1 .. 1 000 000)
+ * microseconds, adds one to the ps_device_timeouts counter and the kernel returns,
+ * leaving the context usable.  Asynchronous on `stream`. */
+PS_API int32_t ps_wait_selftest(uint32_t limit_us, void* stream);
+
 /* Drop-in for _rope(x, cosine, sine) (wan.py:58-63) on a strided 4-D tensor.
  *   x, out:   [B, L, H, D] with element strides x_strides[0..2], out_strides[0..2]
  *             (the D stride is 1); x and out may not overlap unless equal.

@@ -32,7 +32,7 @@ KERNEL_AUTO, KERNEL_ROWS, KERNEL_BULK = 0, 1, 2
 ROPE_SPLIT, ROPE_INTERLEAVED = 0, 1
 
 EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
-           "ps_device_timeouts", "ps_rope", "ps_rope_validate",
+           "ps_device_timeouts", "ps_wait_selftest", "ps_rope", "ps_rope_validate",
            "ps_table_prep_validate", "ps_qk_norm_rope_tables", "ps_rope_tables", "ps_rope_tables_validate")
 
 
@@ -147,6 +147,8 @@ def load() -> ctypes.CDLL:
     lib.ps_qk_norm_rope_kv.argtypes = [ctypes.c_void_p, ctypes.c_void_p]  # (const ps_qk_prep_args*, stream)
     lib.ps_device_timeouts.restype = ctypes.c_int32
     lib.ps_device_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
+    lib.ps_wait_selftest.restype = ctypes.c_int32
+    lib.ps_wait_selftest.argtypes = [ctypes.c_uint32, ctypes.c_void_p]
     i64p = ctypes.POINTER(ctypes.c_int64)
     rope_args = [ctypes.c_int32, ctypes.c_void_p, i64p, ctypes.c_void_p, ctypes.c_void_p, i64p, ctypes.c_void_p,
                  i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]

@@ -360,17 +360,28 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Waits for the phase of `parity` to complete, giving up after kWaitNs.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for the phase of `parity` to complete, giving up after `limit_ns`.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   for (;;) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - start > kWaitNs) {
+    if (global_ns() - start > limit_ns) {
       atomicAdd(&g_wait_timeouts, 1u);
       return false;
     }
+  }
+}
+
+// Self-test of the bounded wait: thread 0 waits on an mbarrier that expects one arrival
+// nobody makes; the wait gives up after `limit_ns`, counts itself in g_wait_timeouts and
+// the kernel returns.  Nothing else is touched.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_wait(&bar, 0, limit_ns);
   }
 }
 
@@ -1087,6 +1098,16 @@ extern "C" int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream)
                               ? ps::launch_typed<__nv_bfloat16>(plan, static_cast<cudaStream_t>(stream))
                               : ps::launch_typed<float>(plan, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "qk_prep launch: %s", cudaGetErrorString(err));
+  return PS_OK;
+}
+
+extern "C" int32_t ps_wait_selftest(uint32_t limit_us, void* stream) {
+  ps::clear_error();
+  if (limit_us < 1 || limit_us > 1000000)
+    return ps::fail(PS_ERR_SHAPE, "limit_us=%u outside [1, 1000000]", limit_us);
+  ps::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(1000ull * limit_us);
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "wait self-test launch: %s", cudaGetErrorString(err));
   return PS_OK;
 }
 

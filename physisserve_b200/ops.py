@@ -518,6 +518,14 @@ def qk_norm_rope_tables(
         _check(_lib.load().ps_qk_norm_rope_tables(ctypes.byref(args), _stream(device)))
 
 
+def wait_selftest(limit_us: int = 20000, device: int | None = None) -> None:
+    """Launch the bounded-wait self-test on ``device`` (default: current): one wait that
+    nothing completes gives up after ``limit_us`` and adds one to ``device_timeouts``."""
+    index = torch.cuda.current_device() if device is None else int(device)
+    with _on_device(index):
+        _check(_lib.load().ps_wait_selftest(int(limit_us), _current_stream(index)))
+
+
 def device_timeouts(reset: bool = True) -> int:
     """Bounded waits of the bulk kernel that ran out on the current device (synchronises)."""
     count = ctypes.c_uint32(0)
