@@ -706,12 +706,15 @@ def run_processor(args):
     cos, sin = wan_rope_tables(D, 64, device=device)
     split = (D - 4 * (D // 6), 2 * (D // 6), 2 * (D // 6))
 
-    # Reference layout: 19 history pages (sink chunk 0 of 3 frames + chunks 7..24), pre-RoPE.
+    # Reference layout: 19 history pages (sink chunk 0 of 3 frames + chunks 7..24), pre-RoPE,
+    # each in the layout its processor publishes: the reference's are transposed views of the
+    # token-major projections, the drop-in's are head-major contiguous.
     pos = window_layout(chunk)
     history = [chunk_id for chunk_id in [0, *range(chunk - 18, chunk)]]
     frames = {c: (3 if c == 0 else 1) for c in history}
     pages = [tuple(torch.randn(1, H, frames[c] * hw, D, generator=g).bfloat16().to(device) for _ in range(2))
              for c in history]
+    view_pages = [tuple(t.transpose(1, 2).contiguous().transpose(1, 2) for t in page) for page in pages]
 
     def frames_table(start, stop):
         out = []
@@ -746,7 +749,7 @@ def run_processor(args):
         q = attn.norm_q(attn.to_q(hidden)).unflatten(2, (H, -1))
         k = attn.norm_k(attn.to_k(hidden)).unflatten(2, (H, -1)).transpose(1, 2)
         v = attn.to_v(hidden).unflatten(2, (H, -1)).transpose(1, 2)
-        k, v = Cache(pages)(k, v)
+        k, v = Cache(view_pages)(k, v)
         q = rope(q, *own).type_as(q).transpose(1, 2)
         k = rope(k.transpose(1, 2), *window).type_as(k).transpose(1, 2)
         out = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).flatten(2)

@@ -105,8 +105,12 @@ class Attention:
         q_rot, k_page = prepare_reference_layout(q, k, heads, _norm_weight(attn.norm_q, C, q.dtype, q.device),
                                                  _norm_weight(attn.norm_k, C, k.dtype, k.device),
                                                  _norm_eps(attn.norm_q, q.dtype), own)
-        k_page = k_page.view(B, L, heads, D).transpose(1, 2)
-        v_page = v.unflatten(2, (heads, -1)).transpose(1, 2)
+        # Pages are published head-major contiguous ([B, heads, tokens, D] with unit strides),
+        # not as transposed views of the token-major rows: the engine's window concat
+        # (Cache, kv_cache.py:51-56) of contiguous pages takes 56 us for a 105 MB window on a
+        # B200, of transposed views 243 us (torch.cat's strided path).  Same values.
+        k_page = k_page.view(B, L, heads, D).transpose(1, 2).contiguous()
+        v_page = v.unflatten(2, (heads, -1)).transpose(1, 2).contiguous()
         k_window, v_window = self.cache(k_page, v_page)  # pages are [B, heads, tokens, head_dim], before RoPE
         k_window = rope(k_window.transpose(1, 2), *window).transpose(1, 2)
         q_rot = q_rot.view(B, L, heads, D).transpose(1, 2)
