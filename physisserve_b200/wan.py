@@ -304,11 +304,17 @@ class RingAttention:
                           _norm_weight(attn.norm_k, C, k.dtype, k.device), _norm_eps(attn.norm_q, q.dtype),
                           freqs_cos, freqs_sin, cache, positions)
         q_rot = q_rot.view(B, L, heads, D).transpose(1, 2)
-        outs = []
-        for b, pos in enumerate(positions):
-            kw, vw = cache.window(pos.chunk)
-            outs.append(F.scaled_dot_product_attention(q_rot[b:b + 1], kw[b:b + 1], vw[b:b + 1]))
-        hidden = torch.cat(outs).transpose(1, 2).flatten(2)
+        if len({cache.window_rows(pos.chunk) for pos in positions}) == 1:
+            # Members whose windows have the same length: one SDPA over the ring views.
+            kw, vw = cache.window(positions[0].chunk)
+            out = F.scaled_dot_product_attention(q_rot, kw, vw)
+        else:
+            outs = []
+            for b, pos in enumerate(positions):
+                kw, vw = cache.window(pos.chunk)
+                outs.append(F.scaled_dot_product_attention(q_rot[b:b + 1], kw[b:b + 1], vw[b:b + 1]))
+            out = torch.cat(outs)
+        hidden = out.transpose(1, 2).flatten(2)
         return attn.to_out[1](attn.to_out[0](hidden))
 
 
