@@ -168,6 +168,33 @@ def test_fused_small_bit_exact_rope_and_slots(kernel, tile):
     _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rows_eight_heads_per_thread(dtype):
+    """The rows kernel's V=8 instantiation (compiled, never the automatic choice): 16 heads,
+    one 32-thread (bf16) or 64-thread (fp32) row group per token."""
+    H, D, gh, gw = 16, 128, 4, 6
+    C = H * D
+    B, frames, capacity = 2, 1, 3
+    L = frames * gh * gw
+    q, k, v = (randn((B, L, C), s, dtype=dtype) for s in (81, 82, 83))
+    wq, wk = norm_weight(C, 84, dtype), norm_weight(C, 85, dtype)
+    cos, sin = oracle.rope_tables(D, 64)
+    split = oracle.axis_dims(D)
+    offsets, slots = [7, 12], [1, 0]
+    got = _run_ring(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, dtype=dtype,
+                    k_pre=True, kernel="rows", heads_per_thread=8)
+    if dtype == torch.bfloat16:
+        _check_streams(q, k, v, wq, wk, cos, sin, split, (gh, gw), offsets, capacity, slots, H, D, got)
+    else:
+        _q_out, ring_k, ring_v, k_pre = got
+        for b in range(B):
+            assert torch.allclose(k_pre[b], oracle.rms_norm(k[b], wk, EPS), rtol=2 ** -20, atol=0)
+            ct, st = token_tables(cos, sin, split, offsets[b], frames, gh, gw)
+            ref_k = oracle.rope(k_pre[b].unflatten(-1, (H, D)), ct[:, None], st[:, None]).flatten(-2)
+            assert torch.equal(ring_k[b, slots[b] * L:(slots[b] + 1) * L], ref_k)
+            assert torch.equal(ring_v[b, slots[b] * L:(slots[b] + 1) * L], v[b])
+
+
 @pytest.mark.parametrize("stages,groups,ctas,release,vstages", [
     (3, 1, 1, 1, 2), (4, 2, 1, 1, 3), (9, 4, 2, 2, 0), (0, 0, 1, 0, 0), (5, 3, 1, 1, 2), (3, 1, 1, 2, 5),
     (7, 3, 1, 2, 16), (13, 3, 1, 4, 9), (17, 2, 1, 8, 8), (0, 6, 1, 0, 0)])
