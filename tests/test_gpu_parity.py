@@ -195,6 +195,43 @@ def test_rows_eight_heads_per_thread(dtype):
             assert torch.equal(ring_v[b, slots[b] * L:(slots[b] + 1) * L], v[b])
 
 
+@pytest.mark.parametrize("heads", [40, 12])       # 10 KB rows -> bulk kernel, 3 KB rows -> rows kernel
+def test_reference_layout_and_sink_modes(heads):
+    """The two specialised call patterns besides the ring prep, on both kernels: the
+    reference-layout prep (RMSNorm Q/K, RoPE(Q) with per-token tables, pre-RoPE K page) and the
+    sink re-rotation (K only, no weights, per-axis tables, written to ring rows)."""
+    D, gh, gw = 128, 5, 8
+    C, hw, B = heads * D, 5 * 8, 2
+    cos, sin = oracle.rope_tables(D, 64)
+    split = oracle.axis_dims(D)
+    q, k = randn((B, hw, C), 91), randn((B, hw, C), 92)
+    wq, wk = norm_weight(C, 93), norm_weight(C, 94)
+    own = [token_tables(cos, sin, split, 9 + b, 1, gh, gw) for b in range(B)]
+    own_cos = torch.stack([t[0] for t in own])[:, :, None]      # [B, L, 1, D], per member
+    own_sin = torch.stack([t[1] for t in own])[:, :, None]
+    q_rot, k_pre = prepare_reference_layout(q.to(DEV), k.to(DEV), heads, wq.to(DEV), wk.to(DEV), EPS,
+                                            (own_cos.to(DEV), own_sin.to(DEV)))
+    torch.cuda.synchronize()
+    for b in range(B):
+        check_bf16_close(k_pre[b].cpu(), oracle.rms_norm(k[b], wk, EPS), f"K page member {b}")
+        want_q = oracle.rope(oracle.rms_norm(q[b], wq, EPS).unflatten(-1, (heads, D)), own[b][0][:, None],
+                             own[b][1][:, None]).flatten(-2)
+        check_rotated_close(q_rot[b].cpu(), want_q, oracle.rms_norm(q[b], wq, EPS), f"rotated Q member {b}")
+
+    # Sink re-rotation: a 3-frame pre-RoPE sink rotated at frame 7, into ring rows 100.. of a pool.
+    frames = 3
+    sink = randn((frames * hw, C), 95)
+    pool = torch.zeros(100 + frames * hw + 20, C, device=DEV, dtype=torch.bfloat16)
+    qk_norm_rope_kv(heads=heads, head_dim=D, seqs=[Seq(0, frames * hw, gh, gw, frame_offset=7, ring_row=100,
+                                                       ring_frames=frames, ring_slot0=0)],
+                    cos=cos.to(DEV), sin=sin.to(DEV), k=sink.to(DEV), k_out=pool, axis_split=split)
+    ct, st = token_tables(cos, sin, split, 7, frames, gh, gw)
+    want = oracle.rope(sink.unflatten(-1, (heads, D)), ct[:, None], st[:, None]).flatten(-2)
+    got = pool.cpu()
+    assert torch.equal(got[100:100 + frames * hw], want)
+    assert not got[:100].any() and not got[100 + frames * hw:].any()
+
+
 @pytest.mark.parametrize("stages,groups,ctas,release,vstages", [
     (3, 1, 1, 1, 2), (4, 2, 1, 1, 3), (9, 4, 2, 2, 0), (0, 0, 1, 0, 0), (5, 3, 1, 1, 2), (3, 1, 1, 2, 5),
     (7, 3, 1, 2, 16), (13, 3, 1, 4, 9), (17, 2, 1, 8, 8), (0, 6, 1, 0, 0)])
