@@ -17,7 +17,12 @@ data path).  Other workloads: ``cfg2`` (1.3B, 18 successive chunks per step),
 steps per step).
 
 ``--impl reference`` times the reference algorithm on the host CPU cores (the oracle's
-restatement of _rope / torch RMSNorm / ring write), rank 0 only.
+restatement of _rope / torch RMSNorm / ring write), rank 0 only.  ``--impl torch`` runs the
+same algorithm as PyTorch ops on the GPU.  Other modes, each printing its own JSON line:
+``--processor [--ltx]`` (a whole self-attention block call: PyTorch ops vs the drop-in vs the
+ring processor), ``--rope-window`` (the _rope drop-in on a 22-frame window), ``--ltx``
+(the LTX-2.5 explicit-table kernels), ``--pipeline`` (2-stage config 5 with NCCL handoff).
+Launches go through ``ops.PrepPlan`` (validated once per step, pointers swapped per launch).
 """
 from __future__ import annotations
 
