@@ -139,6 +139,36 @@ def flat_seq(token_start: int, n_tokens: int, grid_h: int, grid_w: int, frame_of
     return Seq(token_start, n_tokens, grid_h, grid_w, frame_offset, table_row, token_start, frames, 0)
 
 
+def varlen_seqs(cu_seqlens, grids, frame_offsets, *, ring_rows=None, ring_frames: int = 0,
+                ring_slot0s=None) -> list[Seq]:
+    """``Seq`` list of a packed varlen batch (the ``cu_seqlens`` form of the reference's
+    config 4 packing): member i owns rows ``[cu_seqlens[i], cu_seqlens[i+1])`` with latent grid
+    ``grids[i] = (grid_h, grid_w)`` and first frame ``frame_offsets[i]``.  With ``ring_rows``
+    its K/V go to the ring starting at ``ring_rows[i]`` (``ring_frames`` frames, first slot
+    ``ring_slot0s[i]``, default ``frame_offsets[i] % ring_frames``); without, K/V rows mirror
+    the input rows."""
+    cu = [int(c) for c in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
+    n = len(cu) - 1
+    if n < 0 or any(b < a for a, b in zip(cu, cu[1:])) or (cu and cu[0] != 0):
+        raise PrepError("cu_seqlens must start at 0 and be non-decreasing")
+    if len(grids) != n or len(frame_offsets) != n:
+        raise PrepError(f"{n} members need {n} grids and frame offsets")
+    seqs = []
+    for i in range(n):
+        gh, gw = grids[i]
+        tokens = cu[i + 1] - cu[i]
+        if tokens % (gh * gw):
+            raise PrepError(f"member {i}: {tokens} tokens are not whole frames of {gh}x{gw}")
+        if ring_rows is None:
+            seqs.append(flat_seq(cu[i], tokens, gh, gw, frame_offsets[i], table_row=cu[i]))
+        else:
+            if ring_frames < 1:
+                raise PrepError("ring_frames must be >= 1 with ring_rows")
+            slot0 = ring_slot0s[i] if ring_slot0s is not None else ring_slot(frame_offsets[i], ring_frames)
+            seqs.append(Seq(cu[i], tokens, gh, gw, frame_offsets[i], cu[i], int(ring_rows[i]), ring_frames, slot0))
+    return seqs
+
+
 def _rows(t: torch.Tensor | None, C: int, name: str):
     """(pointer, row stride, rows) of a token-major [..., C] or [..., H, D] tensor.
 

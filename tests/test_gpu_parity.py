@@ -340,10 +340,8 @@ def test_config4_varlen_mixed_chunks(kernel):
     cos, sin = oracle.rope_tables(D, 1024)
     split = oracle.axis_dims(D)
     rows = capacity * hw
-    seqs = []
-    for n, i in enumerate(order):
-        seqs.append(Seq(cu[n], frames[i] * hw, gh, gw, frame_offset=offsets[i], ring_row=i * rows,
-                        ring_frames=capacity, ring_slot0=offsets[i] % capacity))
+    seqs = ops.varlen_seqs(torch.tensor(cu), [(gh, gw)] * 16, [offsets[i] for i in order],
+                           ring_rows=[i * rows for i in order], ring_frames=capacity)
     dq, dk, dv = q.to(DEV), k.to(DEV), v.to(DEV)
     q_out = torch.empty_like(dq)
     ring_k = torch.zeros(16 * rows, C, device=DEV, dtype=torch.bfloat16)

@@ -115,3 +115,25 @@ def test_rope_shape_checks():
         ops.rope(x, torch.zeros(1, 5, 1, 128), torch.zeros(1, 5, 1, 128))
     with pytest.raises(PrepError, match="B, L, H, D"):
         ops.rope(x[0], torch.zeros(1, 4, 1, 128), torch.zeros(1, 4, 1, 128))
+
+
+def test_varlen_seqs_from_cu_seqlens():
+    """BASELINE config 4 packing: 4 first chunks (3x22x40) then 12 steady chunks (1x22x40)."""
+    lengths = [2640] * 4 + [880] * 12
+    cu = torch.tensor([0, *torch.tensor(lengths).cumsum(0).tolist()])
+    grids = [(22, 40)] * 16
+    offsets = [0] * 4 + list(range(3, 15))
+    rows = 12 * 880
+    seqs = ops.varlen_seqs(cu, grids, offsets, ring_rows=[i * rows for i in range(16)], ring_frames=12)
+    assert [s.token_start for s in seqs] == cu[:-1].tolist()
+    assert [s.n_tokens for s in seqs] == lengths
+    assert [s.ring_slot0 for s in seqs] == [o % 12 for o in offsets]
+    assert all(s.ring_row == i * rows and s.ring_frames == 12 for i, s in enumerate(seqs))
+    flat = ops.varlen_seqs(cu, grids, offsets)
+    assert all(s.ring_row == s.token_start and s.table_row == s.token_start for s in flat)
+    with pytest.raises(PrepError):
+        ops.varlen_seqs([0, 881], [(22, 40)], [3])                  # not whole frames
+    with pytest.raises(PrepError):
+        ops.varlen_seqs([0, 880, 440], [(22, 40)] * 2, [3, 4])      # decreasing
+    with pytest.raises(PrepError):
+        ops.varlen_seqs([0, 880], [(22, 40)], [3], ring_rows=[0])  # ring without frames
