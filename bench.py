@@ -510,7 +510,7 @@ def run_pipeline(args):
     """
     import torch.distributed as dist
 
-    from physisserve_b200.ops import Seq, qk_norm_rope_kv
+    from physisserve_b200.ops import PrepPlan, Seq
     from physisserve_b200.parallel import PipelineLayout, pipeline_tick, stage_blocks
     from physisserve_b200.wan import wan_rope_tables
 
@@ -544,12 +544,14 @@ def run_pipeline(args):
     seqs = [Seq(i * hw, hw, spec["grid"][1], spec["grid"][2], frame_offset=o, ring_row=i * rows,
                 ring_frames=capacity, ring_slot0=o % capacity) for i, o in enumerate(offsets)]
     launches = [0]
+    # One plan per rank: every block launch swaps in its Q source and norm weights.
+    plan = PrepPlan(heads=heads, head_dim=D, seqs=seqs, cos=cos, sin=sin, q=hidden, k=k, v=v, q_weight=wq[0],
+                    k_weight=wk[0], eps=1e-6, q_out=out, k_out=ring_k, v_out=ring_v)
 
     def run_blocks(h):
         src = h
         for b in range(len(blocks)):
-            qk_norm_rope_kv(heads=heads, head_dim=D, seqs=seqs, cos=cos, sin=sin, q=src, k=k, v=v, q_weight=wq[b],
-                            k_weight=wk[b], eps=1e-6, q_out=out, k_out=ring_k, v_out=ring_v)
+            plan.launch(q=src, q_weight=wq[b], k_weight=wk[b])
             launches[0] += 1
             src = out
         return out
