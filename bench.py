@@ -2,32 +2,35 @@
 """Benchmark of the B200 Wan self-attention prep hot path (RMSNorm + 3D RoPE + KV ring write).
 
 Metric: rotated Q/K tokens per second (one token = all heads of Q and K of one position,
-with its V row copied into the ring), whole job, plus the fused kernel's fraction of the
-measured HBM bandwidth.
+with its V row copied into the ring; one token of one (block, denoising step) cell), whole
+job, plus the fused kernel's fraction of the measured HBM bandwidth.
 
-Default workload ``cfg3`` (Wan2.1-14B same-block batching): 8 streams
-of q, k, v [1560, 40, 128] bf16 ~N(0,1) on a 1x30x52 latent grid, per-stream frame
-offsets drawn from U{3..40}, each stream with a ring of 12 frames written at slot =
-offset mod 12.  One step is one fused launch over the 8-stream batch (one block call);
-successive steps advance every stream by one chunk (offset + 1).  Inputs (384 MB per
-step, two alternating sets) exceed the 126 MB L2, so no flush is needed between steps.
-Under torchrun each rank runs its own 8 streams (weak scaling, no collective on the
-data path).  Other workloads: ``cfg2`` (1.3B, 18 successive chunks per step),
-``cfg4`` (varlen mixed chunks), ``cfg5`` (64 streams sharded over ranks, 30 blocks x 4
-steps per step).
+Default workload ``cfg5`` (the 64-stream Wan2.1-1.3B serving sweep):
+64 streams of q, k, v [1560, 12, 128] bf16 ~N(0,1) on a 1x30x52 latent grid, frame
+offsets U{3..100}, each stream with a ring of 12 frames at slot = offset mod 12.  Streams
+are sharded over ranks (stream i -> rank i mod N, strong scaling: the total work is fixed).
+One step is one chunk of every stream through 30 blocks x 4 denoising steps = 120 fused
+launches (each block with its own RMSNorm weights), launched through ``ops.PrepPlan``.
+The line also carries a nested ``cfg3`` record: BASELINE config 3 (Wan2.1-14B same-block
+batch, 8 streams x [1560, 40, 128], the bulk kernel and the config of the >= 80 % target),
+timed on every rank.  Inputs rotate over sets larger than the 126 MB L2, so no flush is
+needed.  Other workloads: ``--workload cfg2|cfg3|cfg4``.
 
-``--impl reference`` times the reference algorithm on the host CPU cores (the oracle's
-restatement of _rope / torch RMSNorm / ring write), rank 0 only.  ``--impl torch`` runs the
-same algorithm as PyTorch ops on the GPU.  Other modes, each printing its own JSON line:
-``--processor [--ltx]`` (a whole self-attention block call: PyTorch ops vs the drop-in vs the
-ring processor), ``--rope-window`` (the _rope drop-in on a 22-frame window), ``--ltx``
-(the LTX-2.5 explicit-table kernels), ``--pipeline`` (2-stage config 5 with NCCL handoff).
-Launches go through ``ops.PrepPlan`` (validated once per step, pointers swapped per launch).
+``--impl reference`` times the reference algorithm on the host CPU cores, rank 0 only: the
+oracle's restatement (pinned bit-exact to the reference's _rope / Cache outputs) of the
+reference's own layout -- RMSNorm, pre-RoPE page, window concat, RoPE of Q and of the whole
+window per block call -- and, beside it, the ring semantics (rotate the chunk once).
+``--impl torch`` runs the same algorithm as PyTorch ops on the GPU.  Other modes, each
+printing its own JSON line: ``--processor [--ltx]`` (a whole self-attention block call),
+``--rope-window`` (the _rope drop-in on a 22-frame window), ``--ltx`` (the LTX-2.5
+explicit-table kernels), ``--pipeline`` (2-stage config 5 with NCCL handoff, checked against
+a serial run of the same blocks).
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import random
 import statistics
@@ -67,7 +70,7 @@ class Workload:
     """Device buffers and launch list of one rank's share of a workload."""
 
     def __init__(self, name, rank, world, device, seed=1234, ring_frames=None, heads_per_thread=0, streams=None,
-                 **tiling):
+                 launch="pdl", **tiling):
         from physisserve_b200.wan import wan_rope_tables
 
         spec = dict(WORKLOADS[name])
@@ -76,6 +79,7 @@ class Workload:
         if streams:
             spec["streams"] = streams
         self.tiling = dict(heads_per_thread=heads_per_thread, **tiling)
+        self.launch = launch
         self.name, self.spec, self.device = name, spec, device
         self.heads, self.head_dim = spec["heads"], spec["head_dim"]
         self.C = self.heads * self.head_dim
@@ -147,7 +151,7 @@ class Workload:
 
         first = step * self.launches_per_step
         common = dict(heads=self.heads, head_dim=self.head_dim, cos=self.cos, sin=self.sin, eps=1e-6,
-                      q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v, **self.tiling)
+                      q_out=self.q_out, k_out=self.ring_k, v_out=self.ring_v, launch=self.launch, **self.tiling)
         if self.name == "cfg2":
             if self._chunk_plans is None:
                 q, k, v = self.inputs[0]
@@ -300,12 +304,34 @@ def ncu_traffic(workload):
 # --------------------------------------------------------------------------------------
 # CPU reference path (oracle restatement, host cores)
 # --------------------------------------------------------------------------------------
-class CpuReference:
-    """The reference algorithm for one stream chunk on the host CPU: torch RMSNorm of Q and K
-    over H*D, per-token tables sliced from the per-axis tables (WanDiT._frames_table),
-    _rope on Q and K, and the ring write of rotated K and V at slot = offset mod capacity."""
+CPU_STREAMS = 8  # streams of the workload sampled per CPU step
 
-    def __init__(self, spec, seed=99):
+
+def stream_chunk(frames: int, offset: int) -> int:
+    """Request chunk of a stream chunk at latent frame ``offset`` (Chunks.start, chunks.py:35-40:
+    chunk 0 spans the first 3 frames at 0, chunk c >= 1 starts at 3 + (c - 1))."""
+    return 0 if offset == 0 and frames == 3 else offset - 2
+
+
+class CpuReference:
+    """The reference's algorithm for a sample of the workload's stream chunks on the host CPU,
+    all host threads, in two layouts.
+
+    * ``reference`` -- the reference's own per-block-call work (_Attention.__call__ lines
+      104-109 with the engine's Cache, kv_cache.py:51-56): RMSNorm of Q and K over H*D, the
+      pre-RoPE page appended to the chunk's history window (sink + up to 18 recent chunks,
+      history_chunks, kv_cache.py:32-35) by torch.cat, _rope of Q with the chunk's table and of
+      the WHOLE window with the window table.  The per-token tables are built once per chunk, as
+      WanDiT._rotary caches them, and are not timed.
+    * ``ring`` -- the ring semantics this repository implements: RMSNorm, _rope of Q and of the
+      chunk's K once, rotated K and V written at slot = offset mod capacity.
+
+    Both run the oracle's restatement (oracle/wan_prep.py), whose _rope, Cache and window
+    positions are pinned bit-exact to outputs recorded from the reference's own code.
+    One step = one block call of each of the ``CPU_STREAMS`` sampled streams.
+    """
+
+    def __init__(self, spec, seed=99, streams=CPU_STREAMS):
         from oracle import wan_prep as oracle
 
         self.oracle = oracle
@@ -314,36 +340,79 @@ class CpuReference:
         torch.set_num_threads(self.threads)
         heads, D = spec["heads"], spec["head_dim"]
         frames, gh, gw = spec["grid"]
-        self.gh, self.gw, self.hw = gh, gw, gh * gw
+        self.heads, self.gh, self.gw, self.hw = heads, gh, gw, gh * gw
         C = heads * D
-        L = frames * self.hw
+        rng = random.Random(seed)
+        lo, hi = spec["offsets"]
+        n = min(streams, spec["streams"])
+        self.members = []  # (frames, offset) per sampled stream
+        for i in range(n):
+            if spec.get("first_chunks", 0) > i:
+                self.members.append((3, 0))
+            elif spec["streams"] == 1:  # cfg2: successive chunks of one stream
+                self.members.append((frames, lo + i))
+            else:
+                self.members.append((frames, rng.randint(lo, hi)))
         g = torch.Generator().manual_seed(seed)
-        self.q, self.k, self.v = (torch.randn(1, L, C, generator=g).bfloat16() for _ in range(3))
         self.wq, self.wk = ((torch.rand(C, generator=g) + 0.5).bfloat16() for _ in range(2))
-        self.cos, self.sin = oracle.rope_tables(D, 4096)
+        max_frame = max(o + f for f, o in self.members) + 8
+        self.cos, self.sin = oracle.rope_tables(D, max(max_frame, gh, gw))
         self.split = oracle.axis_dims(D)
         self.capacity = spec["capacity"]
-        self.ring_k = torch.zeros(1, self.capacity * self.hw, C, dtype=torch.bfloat16)
-        self.ring_v = torch.zeros_like(self.ring_k)
-        self.tokens = L
-        self.offset = spec["offsets"][0]
+        # Inputs per sampled stream, and pre-RoPE history pages shared by all streams (their
+        # values do not change the work): the sink chunk (3 frames) and 18 one-frame chunks.
+        self.inputs = [tuple(torch.randn(1, f * self.hw, C, generator=g).bfloat16() for _ in range(3))
+                       for f, _ in self.members]
+        page = lambda f: tuple(torch.randn(1, heads, f * self.hw, D, generator=g).bfloat16() for _ in range(2))
+        self.sink_page = page(3)
+        self.recent_pages = [page(1) for _ in range(oracle.HISTORY_CHUNKS)]
+        self.tables = [self._tables(f, o) for f, o in self.members]
+        self.ring_k = [torch.zeros(1, self.capacity * self.hw, C, dtype=torch.bfloat16) for _ in self.members]
+        self.ring_v = [torch.zeros_like(r) for r in self.ring_k]
+        self.tokens = sum(f * self.hw for f, _ in self.members)
+        self.window_tokens = sum(t["window_tokens"] for t in self.tables)
 
-    def step(self):
+    def _tables(self, frames, offset):
         o = self.oracle
-        self.offset += 1
-        o.prep_ring(self.q, self.k, self.v, self.wq, self.wk, 1e-6, self.cos, self.sin, self.split, self.gh, self.gw,
-                    [self.offset], self.ring_k, self.ring_v, [self.offset % self.capacity])
+        chunk = stream_chunk(frames, offset)
+        geometry = o.Chunks((1, 16, 1, self.gh, self.gw), chunk + 1, o.WAN_FIRST_FRAMES)
+        history = o.history_chunks(chunk)
+        first, start, stop = o.window_frames(geometry, chunk, len(history))
+        pages = []
+        for page in history:
+            pages.append(self.sink_page if page == 0 else self.recent_pages[page % o.HISTORY_CHUNKS])
+        own = o.frames_table(self.cos, self.sin, self.split, start, stop, self.gh, self.gw)
+        window = o.frames_table(self.cos, self.sin, self.split, first, stop, self.gh, self.gw)
+        return {"own": own, "window": window, "pages": pages, "window_tokens": (stop - first) * self.hw}
+
+    def step_reference(self):
+        o = self.oracle
+        for (q, k, v), t in zip(self.inputs, self.tables):
+            o.prep_reference_layout_heads(q, k, v, self.wq, self.wk, 1e-6, t["own"], t["window"], t["pages"],
+                                          self.heads)
         return self.tokens
 
-    def sample(self, seconds=10.0, min_steps=3):
-        self.step()  # warm
+    def step_ring(self):
+        o = self.oracle
+        for (q, k, v), (f, off), rk, rv in zip(self.inputs, self.members, self.ring_k, self.ring_v):
+            o.prep_ring(q, k, v, self.wq, self.wk, 1e-6, self.cos, self.sin, self.split, self.gh, self.gw, [off], rk,
+                        rv, [off % self.capacity])
+        return self.tokens
+
+    def sample(self, step, seconds=10.0, min_steps=2):
+        step()  # warm
         steps, tokens = 0, 0
         t0 = time.perf_counter()
         while steps < min_steps or time.perf_counter() - t0 < seconds:
-            tokens += self.step()
+            tokens += step()
             steps += 1
         elapsed = time.perf_counter() - t0
         return tokens / elapsed, steps, elapsed
+
+    def describe(self):
+        return (f"{len(self.members)} stream chunks of {self.spec['grid'][0] * self.hw} tokens per step "
+                f"(H={self.heads}, D={self.spec['head_dim']}; frame offsets {[o for _, o in self.members]}; "
+                f"{self.window_tokens} window keys re-rotated per step in the reference layout)")
 
 
 def cpu_model():
@@ -356,6 +425,21 @@ def cpu_model():
     return "unknown"
 
 
+def bench_config(args, world):
+    """The ``config`` object of a bench line: the same for this repository's arm and the
+    reference arm of the same command line."""
+    spec = WORKLOADS[args.workload]
+    streams = args.streams or spec["streams"]
+    per_gpu = -(-streams // world) if args.workload == "cfg5" else streams
+    return {"workload": args.workload, "desc": spec["desc"], "model": spec["model"], "streams": streams,
+            "streams_per_gpu": per_gpu, "heads": spec["heads"], "head_dim": spec["head_dim"],
+            "grid": list(spec["grid"]), "ring_frames": args.ring_frames or spec["capacity"],
+            "launches_per_step": args.cells or spec["launches"],
+            "parallelism": f"streams sharded, dp{world}" if args.workload == "cfg5" else f"replicas, dp{world}",
+            "l2": "inputs larger than L2 (rotating input sets), no flush",
+            "launch": args.launch}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -363,23 +447,26 @@ def run_reference(args):
     spec = WORKLOADS[args.workload]
     ref = CpuReference(spec)
     for _ in range(args.warmup):
-        ref.step()
+        ref.step_reference()
     t0 = time.perf_counter()
     tokens = 0
     for _ in range(args.steps):
-        tokens += ref.step()
+        tokens += ref.step_reference()
     elapsed = time.perf_counter() - t0
     value = tokens / elapsed
+    ring_value, ring_steps, ring_s = ref.sample(ref.step_ring, seconds=min(10.0, elapsed))
     line = {
         "impl": "reference", "metric": "rotated_qk_tokens_per_s", "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
+        "scaling": "strong" if args.workload == "cfg5" else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": args.workload, "desc": spec["desc"],
-                   "sample": f"one stream chunk of {ref.tokens} tokens per step (H={spec['heads']}, D=128)"},
+        "config": bench_config(args, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
-                         "sample": f"{args.steps} steps x 1 stream chunk ({ref.tokens} tokens)",
-                         "cpu": cpu_model()},
+                         "layout": "reference (window concat + RoPE of the whole window per block call)",
+                         "sample": f"{args.steps} steps x {ref.describe()}", "cpu": cpu_model()},
+        "ring_semantics": {"value": ring_value, "unit": "tokens/s", "steps": ring_steps, "seconds": ring_s,
+                           "layout": "ring (chunk rotated once, K/V written at slot = offset mod capacity)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -389,6 +476,53 @@ def run_reference(args):
 # --------------------------------------------------------------------------------------
 # GPU arm
 # --------------------------------------------------------------------------------------
+def _time_steps(work, steps, warmup, world, graph=None):
+    """Device time of ``steps`` steps of ``work`` on the current stream after ``warmup``
+    (barrier + synchronize on both sides); returns (ms over all steps on this rank, launches)."""
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        if graph is not None:
+            graph.replay()
+            return work.launches_per_step
+        return work.run_step(i)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    begin.record(stream)
+    launches = 0
+    for i in range(steps):
+        launches += step(warmup + i)
+    finish.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return begin.elapsed_time(finish), launches
+
+
+def run_cfg3_record(args, rank, world, device):
+    """BASELINE config 3 (the >= 80 % target's config, bulk kernel) timed on every rank: each
+    rank runs its own 8-stream 14B batch, one fused launch per step."""
+    work = Workload("cfg3", rank, world, device, launch=args.launch)
+    steps = max(20, args.steps)
+    ms, launches = _time_steps(work, steps, max(3, args.warmup), world)
+    launch_ms = max_over_ranks(ms / launches, world, device)
+    peak, _ = measured_peak()
+    achieved = work.bytes_per_launch / (launch_ms / 1000.0) / 1e9
+    tokens_all = sum(gather_objects(work.tokens_per_launch * launches, world))
+    record = {"value": tokens_all / (max_over_ranks(ms, world, device) / 1000.0), "unit": "tokens/s",
+              "desc": WORKLOADS["cfg3"]["desc"], "launches": launches, "launch_us": launch_ms * 1000.0,
+              "bytes_per_launch": work.bytes_per_launch, "achieved_gbs": achieved, "frac": achieved / peak,
+              "traffic": ncu_traffic("cfg3"), "kernel": "bulk (automatic for 10 KB rows)",
+              "scaling": "weak (each rank its own 8 streams)"}
+    del work
+    torch.cuda.empty_cache()
+    return record
+
+
 def run_ours(args):
     rank, world, local = init_dist()
     device = torch.device("cuda", local)
@@ -397,9 +531,9 @@ def run_ours(args):
 
     _lib.load()
     work = Workload(args.workload, rank, world, device, ring_frames=args.ring_frames, streams=args.streams,
-                    heads_per_thread=args.heads_per_thread, kernel=args.kernel, stages=args.stages,
-                    groups=args.groups, ctas_per_sm=args.ctas_per_sm, row_threads=args.row_threads,
-                    release=args.release, vstages=args.vstages, vdepth=args.vdepth)
+                    heads_per_thread=args.heads_per_thread, launch=args.launch, kernel=args.kernel,
+                    stages=args.stages, groups=args.groups, ctas_per_sm=args.ctas_per_sm,
+                    row_threads=args.row_threads, release=args.release, vstages=args.vstages, vdepth=args.vdepth)
     if args.cells:
         work.launches_per_step = args.cells
         work.tokens_per_step = work.tokens_per_launch * args.cells
@@ -449,10 +583,18 @@ def run_ours(args):
     tokens_all = sum(gather_objects(work.tokens_per_step * args.steps, world))
     value = tokens_all / (total_ms / 1000.0)
 
-    # Roofline of the fused kernel: algorithmic bytes per launch / average launch time.
-    launch_ms = sum(step_ms) / (args.steps * work.launches_per_step)
+    # Roofline of the fused kernel: algorithmic bytes per launch / average launch time (the
+    # slowest rank's, since every rank's launch moves the same bytes).
+    launch_ms = max_over_ranks(sum(step_ms) / (args.steps * work.launches_per_step), world, device)
     achieved = work.bytes_per_launch / (launch_ms / 1000.0) / 1e9
     peak, peak_src = measured_peak()
+    if graph is not None:
+        del graph
+
+    # BASELINE config 3 on every rank (nested record).
+    cfg3 = None
+    if args.workload != "cfg3" and not args.no_cfg3:
+        cfg3 = run_cfg3_record(args, rank, world, device)
 
     # End to end through the public API: pinned host inputs -> device -> prep -> q' to host.
     e2e = None if args.no_e2e else run_e2e(args, work, world, device, stream)
@@ -461,27 +603,30 @@ def run_ours(args):
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         ref = CpuReference(WORKLOADS[args.workload])
-        cpu_value, cpu_steps, cpu_s = ref.sample(args.cpu_seconds)
+        cpu_value, cpu_steps, cpu_s = ref.sample(ref.step_reference, args.cpu_seconds)
+        ring_value, ring_steps, ring_s = ref.sample(ref.step_ring, min(5.0, args.cpu_seconds))
         cpu = {"value": cpu_value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
-               "sample": f"{cpu_steps} stream chunks of {ref.tokens} tokens in {cpu_s:.1f} s", "cpu": cpu_model()}
+               "layout": "reference (window concat + RoPE of the whole window per block call)",
+               "sample": f"{cpu_steps} steps in {cpu_s:.1f} s, each {ref.describe()}", "cpu": cpu_model(),
+               "ring_semantics": {"value": ring_value, "unit": "tokens/s",
+                                  "sample": f"{ring_steps} steps in {ring_s:.1f} s"}}
 
     if rank == 0:
-        spec = WORKLOADS[args.workload]
-        config_extra = {"ring_frames_override": args.ring_frames} if args.ring_frames else {}
+        config = bench_config(args, world)
+        config.update({"tokens_per_launch": work.tokens_per_launch, "cuda_graph": bool(args.graph)})
+        if args.ring_frames:
+            config["ring_frames_override"] = args.ring_frames
         line = {
             "metric": "rotated_qk_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "strong" if args.workload == "cfg5" else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": args.workload, "desc": spec["desc"], "model": spec["model"],
-                       "tokens_per_launch": work.tokens_per_launch, "launches_per_step": work.launches_per_step,
-                       "streams_per_gpu": len(work.tokens), "heads": work.heads, "head_dim": work.head_dim,
-                       "ring_frames": work.capacity, "parallelism": f"streams sharded, dp{world}",
-                       "l2": "inputs larger than L2 (two alternating sets), no flush",
-                       "cuda_graph": bool(graph is not None)},
+            "config": config,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic(args.workload), "peak_source": peak_src,
-                         "bytes_per_launch": work.bytes_per_launch, "launch_us": launch_ms * 1000.0},
+                         "bytes_per_launch": work.bytes_per_launch, "launch_us": launch_ms * 1000.0,
+                         "kernel": "rows" if work.C * 2 < 8192 else "bulk"},
+            "cfg3": cfg3,
             "clocks": all_clocks[0] if world == 1 else {"per_rank": all_clocks, **all_clocks[0]},
             "e2e": e2e,
             "gpu_launches": launches,
@@ -489,8 +634,6 @@ def run_ours(args):
             "gpu": torch.cuda.get_device_name(device),
         }
         emit(line)
-    if graph is not None:
-        del graph
     if world > 1:
         import torch.distributed as dist
 
@@ -499,19 +642,24 @@ def run_ours(args):
 
 
 def run_pipeline(args):
-    """BASELINE config 5, pipelined: 2-stage pipelines of 15 blocks per GPU over NCCL send/recv.
+    """BASELINE config 5, pipelined: 2-stage pipelines of 15 blocks per GPU over NCCL.
 
-    Ranks form pipelines of two consecutive ranks; the 64 streams are sharded over pipelines
-    and split into two micro-batches per pipeline.  Each tick every stage runs its 15 blocks
-    (one fused prep launch per block over the micro-batch's streams, Q taken from the hidden
-    state it holds) and then hands the hidden state [tokens, 1536] bf16 to the other stage with
-    one grouped send/recv (physisserve_b200.parallel.pipeline_tick).  4 denoising steps x 2
-    stages = 8 ticks move a micro-batch through the 30 blocks x 4 steps of a chunk.
+    Ranks form pipelines of two consecutive ranks (StageEqual's contiguous split of the 30
+    blocks, engine/strategies/stage_equal.py:21-57); the 64 streams are sharded over
+    pipelines and each pipeline's streams split into 4 micro-batches, two per stage ("lanes").
+    Each tick a stage runs its 15 blocks on lane 0 (one fused prep launch per block, Q taken
+    from the hidden state), posts lane 0's handoff to the other stage, then runs lane 1 while
+    lane 0's hidden state and latent are in flight, and posts lane 1's.  A lane waits for its
+    received state only when it next runs (physisserve_b200.parallel.Transport, the reference's
+    asynchronous Distributed transport, engine/transport.py:84-156): the hidden state
+    [tokens, 1536] bf16 and the latent travel as one NCCL message per lane.  After the timed
+    ticks, 8 more ticks from the seeded start (4 denoising steps x 2 stages) are checked
+    bit for bit against one GPU running the same 120 block launches of each micro-batch in order.
     """
     import torch.distributed as dist
 
     from physisserve_b200.ops import PrepPlan, Seq
-    from physisserve_b200.parallel import PipelineLayout, pipeline_tick, stage_blocks
+    from physisserve_b200.parallel import PipelineLayout, Transport, stage_blocks
     from physisserve_b200.wan import wan_rope_tables
 
     rank, world, local = init_dist()
@@ -521,72 +669,146 @@ def run_pipeline(args):
         raise SystemExit("--pipeline needs an even number of GPUs (2-stage pipelines)")
     layout = PipelineLayout(world=world, stages=2)
     spec = WORKLOADS["cfg5"]
-    streams = layout.streams(spec["streams"], rank)
-    micro = streams[layout.stage_of(rank)::2]  # the micro-batch this stage starts with
     heads, D = spec["heads"], spec["head_dim"]
-    C, hw = heads * D, spec["grid"][1] * spec["grid"][2]
-    T = len(micro) * hw
-    blocks = stage_blocks(layout.stage_of(rank), 2, 30)
-    g = torch.Generator().manual_seed(77 + rank)
-    hidden = torch.randn(T, C, generator=g).bfloat16().to(device)
-    k = torch.randn(T, C, generator=g).bfloat16().to(device)
-    v = torch.randn(T, C, generator=g).bfloat16().to(device)
-    wq = [(torch.rand(C, generator=g) + 0.5).bfloat16().to(device) for _ in blocks]
-    wk = [(torch.rand(C, generator=g) + 0.5).bfloat16().to(device) for _ in blocks]
+    _, gh, gw = spec["grid"]
+    C, hw = heads * D, gh * gw
+    stage = layout.stage_of(rank)
+    peer = layout.peer(rank, 1)
+    streams = layout.streams(spec["streams"], rank)
+    micro = [streams[m::4] for m in range(4)]   # micro-batches 0, 1 start on stage 0; 2, 3 on stage 1
+    T = len(micro[0]) * hw
+    all_blocks = 30
+    blocks = list(stage_blocks(stage, 2, all_blocks))
     cos, sin = wan_rope_tables(D, 4096, device=device)
     capacity = spec["capacity"]
     rows = capacity * hw
-    ring_k = torch.zeros(len(micro) * rows, C, device=device, dtype=torch.bfloat16)
-    ring_v = torch.zeros_like(ring_k)
-    out = torch.empty(T, C, device=device, dtype=torch.bfloat16)
-    rng = random.Random(5 + rank)
-    offsets = [rng.randint(*spec["offsets"]) for _ in micro]
-    seqs = [Seq(i * hw, hw, spec["grid"][1], spec["grid"][2], frame_offset=o, ring_row=i * rows,
-                ring_frames=capacity, ring_slot0=o % capacity) for i, o in enumerate(offsets)]
-    launches = [0]
-    # One plan per rank: every block launch swaps in its Q source and norm weights.
-    plan = PrepPlan(heads=heads, head_dim=D, seqs=seqs, cos=cos, sin=sin, q=hidden, k=k, v=v, q_weight=wq[0],
-                    k_weight=wk[0], eps=1e-6, q_out=out, k_out=ring_k, v_out=ring_v)
 
-    def run_blocks(h):
-        src = h
-        for b in range(len(blocks)):
-            plan.launch(q=src, q_weight=wq[b], k_weight=wk[b])
+    def seeded(seed, shape, scale=1.0, offset=0.0):
+        g = torch.Generator().manual_seed(seed)
+        return (torch.rand(*shape, generator=g) * scale + offset if scale != 1.0 or offset
+                else torch.randn(*shape, generator=g)).bfloat16().to(device)
+
+    # Every block's norm weights are seeded by the block index (the check runs all 30 blocks).
+    wq = [seeded(1000 + b, (C,), 1.0, 0.5) for b in range(all_blocks)]
+    wk = [seeded(2000 + b, (C,), 1.0, 0.5) for b in range(all_blocks)]
+    latent_shape = (len(micro[0]), 16, 1, 60, 104)    # the chunk's latent travels with the hidden state
+    plans, initial = [], []
+    for m, ids in enumerate(micro):
+        offsets = [random.Random(7 + i).randint(*spec["offsets"]) for i in ids]
+        seqs = [Seq(i * hw, hw, gh, gw, frame_offset=o, ring_row=i * rows, ring_frames=capacity,
+                    ring_slot0=o % capacity) for i, o in enumerate(offsets)]
+        k, v = seeded(300 + m, (T, C)), seeded(400 + m, (T, C))
+        ring_k = torch.zeros(len(ids) * rows, C, device=device, dtype=torch.bfloat16)
+        q0 = seeded(100 + m, (T, C))
+        plans.append(PrepPlan(heads=heads, head_dim=D, seqs=seqs, cos=cos, sin=sin, q=q0, k=k, v=v,
+                              q_weight=wq[0], k_weight=wk[0], eps=1e-6, q_out=torch.empty_like(q0),
+                              k_out=ring_k, v_out=torch.zeros_like(ring_k), launch=args.launch))
+        initial.append((q0, seeded(500 + m, latent_shape)))
+    transport = Transport(device)
+    item_spec = [((T, C), torch.bfloat16), (latent_shape, torch.bfloat16)]
+    launches = [0]
+    stream = torch.cuda.current_stream(device)
+
+    def run_blocks(m, hidden, block_list):
+        out = torch.empty_like(hidden)
+        src = hidden
+        for b in block_list:
+            plans[m].launch(q=src, q_out=out, q_weight=wq[b], k_weight=wk[b])
             launches[0] += 1
             src = out
         return out
 
-    for _ in range(args.warmup):
-        hidden = pipeline_tick(layout, rank, hidden, run_blocks)
+    def fresh_lanes():
+        # lane -> (micro-batch id, Pending of its (hidden, latent))
+        from physisserve_b200.parallel import Pending
+
+        own = (0, 1) if stage == 0 else (2, 3)
+        return [(m, Pending(initial[m])) for m in own]
+
+    def tick(lanes, t, events=None):
+        new_lanes = []
+        for lane, (m, pending) in enumerate(lanes):
+            hidden, latent = pending.wait()
+            if events is not None:
+                events[t][lane][0].record(stream)
+            out = run_blocks(m, hidden, blocks)
+            if events is not None:
+                events[t][lane][1].record(stream)
+            # Lane `lane` of this stage goes to the peer; the peer's same lane comes back.
+            # Both ranks list the two items in the same (stage 0's item first) order.
+            # Lane L holds micro-batch L or L + 2 on either stage, the other one on the peer.
+            other = (m + 2) % 4
+            mine = ("x", rank, peer, item_spec, (out, latent))
+            theirs = ("y", peer, rank, item_spec, None)
+            got = transport.transfer([mine, theirs] if stage == 0 else [theirs, mine])
+            new_lanes.append((other, got["y"]))
+        return new_lanes
+
+    lanes = fresh_lanes()
+    for t in range(args.warmup):
+        lanes = tick(lanes, t)
+    for _, pending in lanes:
+        pending.wait()
+    transport.flush()
     torch.cuda.synchronize()
     dist.barrier()
-    stream = torch.cuda.current_stream(device)
+    events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(2)] for _ in range(args.steps)]
     begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     launches[0] = 0
     torch.cuda.synchronize()
     sampler.start()
     begin.record(stream)
-    for _ in range(args.steps):
-        hidden = pipeline_tick(layout, rank, hidden, run_blocks)
+    for t in range(args.steps):
+        lanes = tick(lanes, t, events)
+    for _, pending in lanes:
+        pending.wait()
     finish.record(stream)
     torch.cuda.synchronize()
     clocks = sampler.stop()
+    transport.flush()
     dist.barrier()
-    ms = max_over_ranks(begin.elapsed_time(finish), world, device)
-    tokens = sum(gather_objects(T * len(blocks) * args.steps, world))
+    local_ms = begin.elapsed_time(finish)
+    prep_ms = sum(events[t][lane][0].elapsed_time(events[t][lane][1]) for t in range(args.steps) for lane in range(2))
+    ms = max_over_ranks(local_ms, world, device)
+    prep_tick_us = max_over_ranks(1000 * prep_ms / args.steps, world, device)
+    timed_launches = launches[0]
+
+    # Correctness: 8 ticks from the seeded start, then each stage holds its own two
+    # micro-batches again, each through 4 x 30 blocks; compare with the serial run.
+    lanes = fresh_lanes()
+    for t in range(8):
+        lanes = tick(lanes, t)
+    finals = {m: pending.wait()[0] for m, pending in lanes}
+    transport.flush()
+    torch.cuda.synchronize()
+    ok = True
+    for m, got in finals.items():
+        order = list(range(all_blocks)) if m < 2 else [*range(15, all_blocks), *range(15)]
+        h = initial[m][0]
+        for _ in range(4):
+            h = run_blocks(m, h, order)
+        ok = ok and bool(torch.equal(got, h))
+    torch.cuda.synchronize()
+    checks = gather_objects(ok, world)
+    tokens = sum(gather_objects(2 * T * len(blocks) * args.steps, world))
     all_clocks = gather_objects(clocks, world)
     if rank == 0:
+        tick_us = 1000 * ms / args.steps
         line = {
             "metric": "rotated_qk_tokens_per_s", "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": "cfg5-pipelined", "desc": "64 streams, 2-stage pipelines x 15 blocks, NCCL "
-                       "send/recv of the [tokens, 1536] bf16 hidden state each tick",
-                       "pipelines": layout.pipelines, "tokens_per_microbatch": T,
-                       "handoff_bytes_per_tick": T * C * 2, "step": "one pipeline tick"},
+            "config": {"workload": "cfg5-pipelined", "desc": "64 streams, 2-stage pipelines x 15 blocks, 2 lanes "
+                       "per stage; hidden state [tokens, 1536] bf16 + latent as one NCCL message per lane per tick",
+                       "pipelines": layout.pipelines, "tokens_per_lane": T, "streams_per_lane": len(micro[0]),
+                       "handoff_bytes_per_tick": 2 * (T * C * 2 + math.prod(latent_shape) * 2),
+                       "step": "one pipeline tick", "launch": args.launch},
+            "tick_us": tick_us, "prep_us_per_tick": prep_tick_us,
+            "handoff_stall_us_per_tick": max(0.0, tick_us - prep_tick_us),
+            "check": "ok" if all(checks) else f"mismatch on ranks {[r for r, c in enumerate(checks) if not c]}",
             "clocks": {"per_rank": all_clocks, **all_clocks[0]},
-            "gpu_launches": launches[0], "e2e": None,
+            "gpu_launches": timed_launches, "e2e": None,
         }
         emit(line)
     dist.destroy_process_group()
@@ -1087,11 +1309,14 @@ def run_rope_window(args):
 
 
 def run_e2e(args, work, world, device, stream):
-    """The public API end to end: every step copies its q, k, v from pinned host memory to the
-    device, runs the fused prep through physisserve_b200.ops.qk_norm_rope_kv and copies the
-    rotated Q back to pinned host memory.  Steps are pipelined on three CUDA streams (copy in,
-    compute, copy out) over two buffer sets, so step i+1's host-to-device copy overlaps step i's
-    compute and device-to-host copy (PCIe is full duplex); the timed region covers all of it."""
+    """The public API end to end: every launch of a step copies its q, k, v from pinned host
+    memory to the device, runs the fused prep through physisserve_b200.ops.qk_norm_rope_kv
+    (with that launch's block weights) and copies the rotated Q back to pinned host memory.
+    Launches are pipelined on three CUDA streams (copy in, compute, copy out) over two buffer
+    sets, so launch i+1's host-to-device copy overlaps launch i's compute and device-to-host
+    copy (PCIe is full duplex); the timed region covers all of it.  The number is bound by the
+    host-to-device copies (3*C*2 bytes per token against 12*C bytes of HBM traffic); in serving,
+    q, k and v are produced on the device by the projections."""
     from physisserve_b200.ops import qk_norm_rope_kv
 
     T, C = work.T, work.C
@@ -1105,24 +1330,28 @@ def run_e2e(args, work, world, device, stream):
     comp_done = [torch.cuda.Event() for _ in range(2)]
     out_done = [torch.cuda.Event() for _ in range(2)]
     used = [False, False]
-    steps = max(3, min(args.steps, args.e2e_steps))
+    per_step = work.launches_per_step
+    steps = max(1, min(args.steps, args.e2e_steps))
 
     def one(i):
         b = i % 2
+        step, cell = divmod(i, per_step)
         with torch.cuda.stream(s_in):
             if used[b]:
-                s_in.wait_event(comp_done[b])  # the compute of step i-2 has read these inputs
+                s_in.wait_event(comp_done[b])  # the compute of launch i-2 has read these inputs
             for h, d in zip(host_in, dev_in[b]):
                 d.copy_(h, non_blocking=True)
             in_done[b].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(in_done[b])
             if used[b]:
-                s_comp.wait_event(out_done[b])  # step i-2's result has left the device
+                s_comp.wait_event(out_done[b])  # launch i-2's result has left the device
             q, k, v = dev_in[b]
-            qk_norm_rope_kv(heads=work.heads, head_dim=work.head_dim, seqs=work.seqs(i), cos=work.cos,
-                            sin=work.sin, q=q, k=k, v=v, q_weight=work.wq[0], k_weight=work.wk[0], eps=1e-6,
-                            q_out=dev_out[b], k_out=work.ring_k, v_out=work.ring_v, **work.tiling)
+            block = cell % work.n_blocks
+            qk_norm_rope_kv(heads=work.heads, head_dim=work.head_dim, seqs=work.seqs(step), cos=work.cos,
+                            sin=work.sin, q=q, k=k, v=v, q_weight=work.wq[block], k_weight=work.wk[block], eps=1e-6,
+                            q_out=dev_out[b], k_out=work.ring_k, v_out=work.ring_v, launch=work.launch,
+                            **work.tiling)
             comp_done[b].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(comp_done[b])
@@ -1138,7 +1367,7 @@ def run_e2e(args, work, world, device, stream):
     begin.record(stream)
     for s in (s_in, s_comp, s_out):
         s.wait_event(begin)
-    for i in range(steps):
+    for i in range(steps * per_step):
         one(i)
     for s in (s_in, s_comp, s_out):
         end_event = torch.cuda.Event()
@@ -1147,10 +1376,12 @@ def run_e2e(args, work, world, device, stream):
     finish.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(begin.elapsed_time(finish), world, device)
-    tokens = T * steps * world
-    return {"value": tokens / (ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": 3 * T * C * 2,
-            "d2h_bytes_per_step": T * C * 2, "steps": steps, "api": "physisserve_b200.ops.qk_norm_rope_kv",
-            "pipelined": "copy-in / compute / copy-out on three streams, two buffer sets"}
+    tokens = sum(gather_objects(T * per_step * steps, world))
+    return {"value": tokens / (ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": 3 * T * C * 2 * per_step,
+            "d2h_bytes_per_step": T * C * 2 * per_step, "steps": steps, "launches_per_step": per_step,
+            "api": "physisserve_b200.ops.qk_norm_rope_kv",
+            "pipelined": "copy-in / compute / copy-out on three streams, two buffer sets",
+            "bound": "host-to-device copy of q, k, v (PCIe); in serving they are produced on the device"}
 
 
 _RESULT_OUT = None
@@ -1177,18 +1408,22 @@ def main(argv=None):
     _reserve_stdout()
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=200)
-    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--steps", type=int, default=30)
+    parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference", "torch"), default="ours",
                         help="ours: the fused kernels; reference: the reference algorithm on host CPU cores; "
                              "torch: the reference algorithm as PyTorch ops on the GPU")
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg5")
+    parser.add_argument("--launch", choices=("pdl", "stream", "pdl_early_inputs"), default="pdl",
+                        help="ps_launch mode of the prep launches (pdl: programmatic dependent launch that "
+                             "waits for the previous kernel before any memory access)")
+    parser.add_argument("--no-cfg3", action="store_true", help="skip the nested config-3 record")
     parser.add_argument("--graph", action="store_true", help="replay each step from a captured CUDA graph")
     parser.add_argument("--streams", type=int, default=None,
                         help="override the workload's stream count (e.g. cfg5 --streams 8 = one rank's share at N=8)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
-    parser.add_argument("--e2e-steps", type=int, default=20)
+    parser.add_argument("--e2e-steps", type=int, default=2, help="steps of the end-to-end leg")
     parser.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     parser.add_argument("--ring-frames", type=int, default=None,
                         help="ring capacity override (smaller device footprint for profiling runs)")

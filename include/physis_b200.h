@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define PS_ABI_VERSION 1
+#define PS_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define PS_API __attribute__((visibility("default")))
@@ -86,6 +86,34 @@ typedef enum ps_kernel {
   PS_KERNEL_BULK = 2   /* persistent CTAs streaming rows through shared memory with cp.async.bulk */
 } ps_kernel;
 
+/* How a ps_qk_norm_rope_kv launch is ordered after the work before it on its stream. */
+typedef enum ps_launch {
+  /* Ordinary stream order: the kernel starts once the previous work on the stream is done. */
+  PS_LAUNCH_STREAM = 0,
+  /* Programmatic dependent launch: the kernel may be scheduled while the previous kernel on
+   * the stream is still finishing, so its launch and set-up overlap that kernel's tail.  Every
+   * thread waits for the previous kernel to complete (griddepcontrol.wait) before its first
+   * global-memory access, so that kernel may produce this call's inputs.  After work that is
+   * not a kernel it behaves like PS_LAUNCH_STREAM. */
+  PS_LAUNCH_PDL = 1,
+  /* As PS_LAUNCH_PDL, but the inputs (q, k, v, k_sink, the weights and the tables) are read
+   * before the wait; only the writes wait.  Valid only when no kernel that may still be running
+   * on the stream writes those inputs: a chain of prep launches over inputs produced earlier,
+   * never a launch whose q is the previous launch's q_out. */
+  PS_LAUNCH_PDL_EARLY_INPUTS = 2
+} ps_launch;
+
+/* What a sequence of a ps_qk_norm_rope_kv call does. */
+typedef enum ps_seq_kind {
+  /* The call's roles: RMSNorm and RoPE of Q and K, rotated K and V to the ring. */
+  PS_SEQ_PREP = 0,
+  /* Re-rotation of a relocated attention sink (the positions WanDiT._rotary gives the sink,
+   * wan.py:254-277): rows token_start .. of args.k_sink hold normalised K before RoPE; they are
+   * rotated at this sequence's positions and written to k_out's ring rows.  No Q, no V, no
+   * RMSNorm.  Needs k_sink and k_out. */
+  PS_SEQ_SINK = 1
+} ps_seq_kind;
+
 /* One sequence of a ps_qk_norm_rope_kv call: a stream's chunk, a batch member
  * of WanDiT.block_batch (wan.py:291-314) or a varlen member. */
 typedef struct ps_seq {
@@ -98,6 +126,8 @@ typedef struct ps_seq {
   int64_t ring_row;     /* first row of the stream's ring in k_out / v_out */
   int32_t ring_frames;  /* ring capacity in frames (> 0) */
   int32_t ring_slot0;   /* slot of the sequence's first frame, in [0, ring_frames) */
+  int32_t kind;         /* ps_seq_kind (0: PS_SEQ_PREP) */
+  int32_t reserved;     /* 0 */
 } ps_seq;
 
 /* Arguments of ps_qk_norm_rope_kv.  Frame f of a sequence (f < n_tokens /
@@ -124,6 +154,9 @@ typedef struct ps_qk_prep_args {
                            have read it */
   int32_t vstages;      /* PS_KERNEL_BULK: shared-memory V stages per CTA; 0 = automatic */
   int32_t vdepth;       /* PS_KERNEL_BULK: V stores kept in flight (1..7, below vstages); 0 = automatic */
+  int32_t weight_f32;   /* 0: q_weight/k_weight are of dtype; 1: they are fp32 (RMSNorm weights kept in
+                           fp32, as for modules in a model's _keep_in_fp32_modules, wan.py:146-148) */
+  int32_t launch;       /* ps_launch */
 
   int64_t in_rows;      /* rows of q, k, v, q_out, k_pre (bounds of token_start + n_tokens) */
   const void* q;  int64_t q_stride;   /* [in_rows, C]; NULL: no Q role */
@@ -141,6 +174,8 @@ typedef struct ps_qk_prep_args {
   void* v_out;  int64_t v_out_stride;  /* V ring pool (same row mapping as k_out) */
   int64_t kv_out_rows;                 /* rows of k_out / v_out */
   void* k_pre;  int64_t k_pre_stride;  /* optional: normalised K before RoPE (same rows as k) */
+  const void* k_sink; int64_t k_sink_stride; /* pre-RoPE K rows of PS_SEQ_SINK sequences; NULL without */
+  int64_t k_sink_rows;                 /* rows of k_sink (bounds of a sink sequence's rows) */
 
   const ps_seq* seqs;   /* host array of n_seqs descriptors */
 } ps_qk_prep_args;
@@ -164,11 +199,16 @@ PS_API int32_t ps_qk_prep_validate(const ps_qk_prep_args* args);
  * role and no weights it is the relocated-sink re-rotation (positions of the
  * sink chosen by WanDiT._rotary, wan.py:254-277).
  *
+ * Sequences of kind PS_SEQ_SINK in the same call re-rotate relocated sinks from
+ * k_sink (one launch for the chunk and the sinks on rows under 8 KB; wider rows
+ * take a second launch on the same stream).
+ *
  * Numerics: RMSNorm accumulates sum(x^2) in fp32, rstd = 1/sqrt(sum/C + eps)
  * with IEEE division and square root, y = (x*rstd)*w rounded once to the
- * element type (torch.nn.RMSNorm); RoPE computes rn(rn(e*c)-rn(o*s)) and
- * rn(rn(e*s)+rn(o*c)) in fp32 from the rounded RMSNorm output and rounds once
- * to the element type (_rope, wan.py:58-63). */
+ * element type (torch.nn.RMSNorm; with fp32 weights the product is formed with
+ * the fp32 weight, as torch does for a bf16 input and an fp32 weight); RoPE
+ * computes rn(rn(e*c)-rn(o*s)) and rn(rn(e*s)+rn(o*c)) in fp32 from the rounded
+ * RMSNorm output and rounds once to the element type (_rope, wan.py:58-63). */
 PS_API int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream);
 
 

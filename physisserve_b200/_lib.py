@@ -12,7 +12,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libphysis_b200.so"
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_SEQS = 64
 
 # ps_status
@@ -30,6 +30,10 @@ TABLE_TOKENS, TABLE_AXES = 0, 1
 KERNEL_AUTO, KERNEL_ROWS, KERNEL_BULK = 0, 1, 2
 # ps_rope_style
 ROPE_SPLIT, ROPE_INTERLEAVED = 0, 1
+# ps_launch
+LAUNCH_STREAM, LAUNCH_PDL, LAUNCH_PDL_EARLY_INPUTS = 0, 1, 2
+# ps_seq_kind
+SEQ_PREP, SEQ_SINK = 0, 1
 
 EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
            "ps_device_timeouts", "ps_wait_selftest", "ps_rope", "ps_rope_validate",
@@ -49,6 +53,8 @@ class PsSeq(ctypes.Structure):
         ("ring_row", ctypes.c_int64),
         ("ring_frames", ctypes.c_int32),
         ("ring_slot0", ctypes.c_int32),
+        ("kind", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -74,6 +80,8 @@ class PsQkPrepArgs(ctypes.Structure):
         ("release", ctypes.c_int32),
         ("vstages", ctypes.c_int32),
         ("vdepth", ctypes.c_int32),
+        ("weight_f32", ctypes.c_int32),
+        ("launch", ctypes.c_int32),
         ("in_rows", ctypes.c_int64),
         ("q", ctypes.c_void_p), ("q_stride", ctypes.c_int64),
         ("k", ctypes.c_void_p), ("k_stride", ctypes.c_int64),
@@ -88,6 +96,8 @@ class PsQkPrepArgs(ctypes.Structure):
         ("v_out", ctypes.c_void_p), ("v_out_stride", ctypes.c_int64),
         ("kv_out_rows", ctypes.c_int64),
         ("k_pre", ctypes.c_void_p), ("k_pre_stride", ctypes.c_int64),
+        ("k_sink", ctypes.c_void_p), ("k_sink_stride", ctypes.c_int64),
+        ("k_sink_rows", ctypes.c_int64),
         ("seqs", ctypes.POINTER(PsSeq)),
     ]
 

@@ -56,6 +56,14 @@ __device__ __forceinline__ void st_vec(void* p, const uint4& v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// Programmatic dependent launch.  pdl_wait blocks the calling thread until the
+// grids this one was launched to depend on have completed and their writes are
+// visible (it returns at once for a grid launched in ordinary stream order);
+// pdl_trigger lets a dependent grid be scheduled once every CTA of this grid has
+// triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (sm_100's paired FP32 instructions).  Each lane of
 // a pair is rounded exactly as the scalar IEEE operation would round it.
@@ -120,6 +128,25 @@ template <> struct Pairs16<float> {
   }
   __device__ __forceinline__ static f32x2 round(f32x2 v) { return v; }
 };
+
+// The RMSNorm weights of one 16-byte activation vector starting at element `off`,
+// as fp32 pairs: one 16-byte load of T, or E/4 float4 loads when the weights are
+// kept in fp32 (`w_f32`; fp32 activations always have fp32 weights).
+template <typename T>
+__device__ __forceinline__ void load_weight_pairs(const void* w, bool w_f32, int64_t off, f32x2* out) {
+  constexpr int E = Vec16<T>::kElems;
+  if (sizeof(T) == 2 && w_f32) {
+    const float* wf = static_cast<const float*>(w) + off;
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(wf + e));
+      out[e / 2] = f2_make(v.x, v.y);
+      out[e / 2 + 1] = f2_make(v.z, v.w);
+    }
+  } else {
+    Pairs16<T>::unpack(ld_keep(static_cast<const T*>(w) + off), out);
+  }
+}
 
 __device__ __forceinline__ f32x2 f2_swap(f32x2 v) {
   float a, b;

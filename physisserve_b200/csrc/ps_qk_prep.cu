@@ -38,6 +38,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <vector>
 
 #include "ps_common.cuh"
 
@@ -59,7 +60,7 @@ struct DevSeq {
   int32_t frame_offset;
   int32_t ring_frames;
   int32_t ring_slot0;
-  int32_t _pad;
+  int32_t kind;       // ps_seq_kind
 };
 
 enum : int32_t {
@@ -70,6 +71,7 @@ enum : int32_t {
   kNormK = 16,
   kKPre = 32,
   kKOut = 64,
+  kSinkSeqs = 128,  // some sequences are PS_SEQ_SINK (rows kernel only)
 };
 
 struct KParams {
@@ -84,7 +86,8 @@ struct KParams {
   void* k_out;
   void* v_out;
   void* k_pre;
-  int64_t q_stride, k_stride, v_stride, q_out_stride, k_out_stride, v_out_stride, k_pre_stride;
+  const void* k_sink;
+  int64_t q_stride, k_stride, v_stride, q_out_stride, k_out_stride, v_out_stride, k_pre_stride, k_sink_stride;
   int32_t head_dim;
   int32_t C;
   int32_t tpr;    // threads per row group
@@ -99,6 +102,8 @@ struct KParams {
   int32_t flags;
   int32_t n_seqs;
   int32_t total;  // tokens over all sequences
+  int32_t w_f32;  // RMSNorm weights are fp32
+  int32_t early;  // PS_LAUNCH_PDL_EARLY_INPUTS: inputs are read before the grid-dependency wait
   float eps;
   float c_f;      // (float)C
   // bulk_kernel only
@@ -217,21 +222,30 @@ __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant
   // The row first, so the loads are issued before the rest of the decode.
   const int sidx = find_seq(p, g);
   const int64_t row = p.seq[sidx].row0 + (g - p.cum[sidx]);
+  // A relocated sink's token: K only, read pre-RoPE from k_sink, no RMSNorm (row group uniform).
+  const bool sink = (flags & kSinkSeqs) && p.seq[sidx].kind == PS_SEQ_SINK;
+  const bool do_q = (flags & kHasQ) && !sink;
+  const bool do_v = (flags & kHasV) && !sink;
+  const bool norm_q = (flags & kNormQ) && !sink;
+  const bool norm_k = (flags & kNormK) && !sink;
+  const bool kpre = (flags & kKPre) && !sink;
 
   int elem_off[V];
 #pragma unroll
   for (int i = 0; i < V; ++i) elem_off[i] = (head0 + i * p.hstep) * p.head_dim + dvec * E;
 
+  if (!p.early) pdl_wait();
   uint4 qv[V], kv[V], vv[V];
   if (active) {
     const T* qrow = static_cast<const T*>(p.q) + row * p.q_stride;
-    const T* krow = static_cast<const T*>(p.k) + row * p.k_stride;
+    const T* krow = sink ? static_cast<const T*>(p.k_sink) + row * p.k_sink_stride
+                         : static_cast<const T*>(p.k) + row * p.k_stride;
     const T* vrow = static_cast<const T*>(p.v) + row * p.v_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      if (flags & kHasQ) qv[i] = ld_stream(qrow + elem_off[i]);
+      if (do_q) qv[i] = ld_stream(qrow + elem_off[i]);
       if (flags & kHasK) kv[i] = ld_stream(krow + elem_off[i]);
-      if (flags & kHasV) vv[i] = ld_stream(vrow + elem_off[i]);
+      if (do_v) vv[i] = ld_stream(vrow + elem_off[i]);
     }
   }
   const Token t = decode_in(p, sidx, g);
@@ -245,24 +259,27 @@ __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant
       ss[j] = __ldg(reinterpret_cast<const unsigned long long*>(p.sin + trow * p.head_dim + 2 * pair));
     }
   }
-  if (active && (flags & kHasV)) {
+  // Every load of this thread is in flight: a dependent launch may be scheduled.
+  pdl_trigger();
+  if (p.early) pdl_wait();  // the previous kernel's writes to the outputs must land first
+  if (active && do_v) {
     T* vout = static_cast<T*>(p.v_out) + t.kv_row * p.v_out_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) st_vec(vout + elem_off[i], vv[i]);
   }
 
   float ssq_q = 0.f, ssq_k = 0.f;
-  if (active && (flags & (kNormQ | kNormK))) {
+  if (active && (norm_q || norm_k)) {
     f32x2 aq = 0, ak = 0;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       f32x2 x[P];
-      if (flags & kNormQ) {
+      if (norm_q) {
         PT::unpack(qv[i], x);
 #pragma unroll
         for (int j = 0; j < P; ++j) aq = f2_fma(x[j], x[j], aq);
       }
-      if (flags & kNormK) {
+      if (norm_k) {
         PT::unpack(kv[i], x);
 #pragma unroll
         for (int j = 0; j < P; ++j) ak = f2_fma(x[j], x[j], ak);
@@ -280,14 +297,14 @@ __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant
   const float rk = rstd_of(ssq_k, p.c_f, p.eps);
   const f32x2 rq2 = f2_make(rq, rq), rk2 = f2_make(rk, rk);
 
-  if (flags & kHasQ) {
+  if (do_q) {
     T* qout = static_cast<T*>(p.q_out) + t.row * p.q_out_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       f32x2 x[P], w[P];
       PT::unpack(qv[i], x);
-      if (flags & kNormQ) {
-        PT::unpack(ld_keep(static_cast<const T*>(p.wq) + elem_off[i]), w);
+      if (norm_q) {
+        load_weight_pairs<T>(p.wq, p.w_f32, elem_off[i], w);
 #pragma unroll
         for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rq2), w[j]));
       }
@@ -299,21 +316,21 @@ __global__ void __launch_bounds__(kMaxThreads) rows_kernel(const __grid_constant
   }
   if (flags & kHasK) {
     T* kout = static_cast<T*>(p.k_out) + t.kv_row * p.k_out_stride;
-    T* kpre = static_cast<T*>(p.k_pre) + t.row * p.k_pre_stride;
+    T* kpre_row = static_cast<T*>(p.k_pre) + t.row * p.k_pre_stride;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       f32x2 x[P], w[P];
       PT::unpack(kv[i], x);
-      if (flags & kNormK) {
-        PT::unpack(ld_keep(static_cast<const T*>(p.wk) + elem_off[i]), w);
+      if (norm_k) {
+        load_weight_pairs<T>(p.wk, p.w_f32, elem_off[i], w);
 #pragma unroll
         for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rk2), w[j]));
       }
       float lo[P], hi[P];
-      if (flags & kKPre) {
+      if (kpre) {
 #pragma unroll
         for (int j = 0; j < P; ++j) f2_split(x[j], lo[j], hi[j]);
-        st_vec(kpre + elem_off[i], (flags & kNormK) ? PT::pack(lo, hi) : kv[i]);
+        st_vec(kpre_row + elem_off[i], norm_k ? PT::pack(lo, hi) : kv[i]);
       }
       if (flags & kKOut) {
 #pragma unroll
@@ -496,7 +513,9 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
 
   if (threadIdx.x < 32) {
     // ---------------- producer ----------------
+    if (threadIdx.x != 0) pdl_trigger();
     if (threadIdx.x == 0) {
+      if (!p.early) pdl_wait();
       const T* qb = static_cast<const T*>(p.q);
       const T* kb = static_cast<const T*>(p.k);
       const T* vb = static_cast<const T*>(p.v);
@@ -525,13 +544,18 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
           if (flags & kHasK) bulk_load(st + p.row_bytes, kb + t.row * p.k_stride, p.row_bytes, &full[s]);
           issued = i + 1;
         }
+        if (i == 0) pdl_trigger();  // loads are in flight: a dependent launch may be scheduled
       }
+      if (n_local == 0) pdl_trigger();
       // Drain: every load issued must have landed before the CTA may exit.
       for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
       for (int i = vissued - SV > 0 ? vissued - SV : 0; i < vissued; ++i) mbar_wait(&vfull[i % SV], (i / SV) & 1);
     }
     return;
   }
+  // Every other thread writes outputs: wait for the kernel this one depends on (if any).
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x < 64) {
     // ---------------- V ring: store each row as soon as it lands ----------------
     if (threadIdx.x == 32 && (flags & kHasV)) {
@@ -569,8 +593,6 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
   const int bar_id = 1 + rg;
   auto sync = [&] { named_sync(bar_id, p.tpr); };
   const int nvec = p.C / E;  // 16-byte vectors per row
-  const T* wqb = static_cast<const T*>(p.wq);
-  const T* wkb = static_cast<const T*>(p.wk);
   // Leader: up to p.defer of this group's store groups stay in flight; k-th token of
   // the group is i = rg + k*groups, its stage i % S is freed once its stores read it.
   int released = 0, committed = 0;
@@ -648,7 +670,7 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
         f32x2 x[P], w[P];
         PT::unpack(*reinterpret_cast<const uint4*>(sq + off), x);
         if (flags & kNormQ) {
-          PT::unpack(ld_keep(wqb + off), w);
+          load_weight_pairs<T>(p.wq, p.w_f32, off, w);
 #pragma unroll
           for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rq2), w[j]));
         }
@@ -662,7 +684,7 @@ __global__ void __launch_bounds__(kBulkMaxConsumers + 64, 1) bulk_kernel(const _
         const uint4 raw = *reinterpret_cast<const uint4*>(sk + off);
         PT::unpack(raw, x);
         if (flags & kNormK) {
-          PT::unpack(ld_keep(wkb + off), w);
+          load_weight_pairs<T>(p.wk, p.w_f32, off, w);
 #pragma unroll
           for (int j = 0; j < P; ++j) x[j] = PT::round(f2_mul(f2_mul(x[j], rk2), w[j]));
         }
@@ -711,7 +733,12 @@ struct Plan {
   int64_t blocks;
   size_t smem;
   int elem_size;
+  int launch;  // ps_launch
 };
+
+// build_plan's answer for a call with PS_SEQ_SINK sequences that the bulk kernel would run:
+// the caller splits it into a launch of the chunk's sequences and a K-only launch of the sinks.
+constexpr int kNeedsSplit = -1;
 
 static int pow2_segment(int tpr) {
   int seg = 1;
@@ -759,10 +786,25 @@ static int sm_count() {
   return 148;
 }
 
-static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
-  clear_error();
+// Validates a call and fills its launch plan.  Sequences of kind PS_SEQ_SINK are accepted
+// when `allow_sinks` (they read K from k_sink; one rows-kernel launch covers them with the
+// chunk's sequences, see kNeedsSplit for the bulk kernel).
+static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only, bool allow_sinks) {
   if (!a) return fail(PS_ERR_NULL, "args is NULL");
   if (a->dtype != PS_BF16 && a->dtype != PS_F32) return fail(PS_ERR_DTYPE, "dtype %d is not PS_BF16 or PS_F32", a->dtype);
+  if (a->weight_f32 != 0 && a->weight_f32 != 1) return fail(PS_ERR_DTYPE, "weight_f32=%d is not 0 or 1", a->weight_f32);
+  if (a->launch < PS_LAUNCH_STREAM || a->launch > PS_LAUNCH_PDL_EARLY_INPUTS)
+    return fail(PS_ERR_SHAPE, "launch mode %d unknown", a->launch);
+  if (a->n_seqs < 1) return fail(PS_ERR_SHAPE, "n_seqs=%d", a->n_seqs);
+  if (a->n_seqs > PS_MAX_SEQS) return fail(PS_ERR_TOO_MANY_SEQS, "n_seqs=%d exceeds PS_MAX_SEQS=%d", a->n_seqs, PS_MAX_SEQS);
+  if (!a->seqs) return fail(PS_ERR_NULL, "seqs is NULL");
+  int n_sink = 0;
+  for (int s = 0; s < a->n_seqs; ++s) {
+    if (a->seqs[s].kind != PS_SEQ_PREP && a->seqs[s].kind != PS_SEQ_SINK)
+      return fail(PS_ERR_SHAPE, "seq %d: kind %d unknown", s, a->seqs[s].kind);
+    n_sink += a->seqs[s].kind == PS_SEQ_SINK;
+  }
+  if (n_sink && !allow_sinks) return fail(PS_ERR_SHAPE, "sink sequences are not accepted here");
   const int es = a->dtype == PS_BF16 ? 2 : 4;
   const int E = 16 / es;
   if (a->heads < 1 || a->head_dim < 2 || (a->head_dim % 2)) return fail(PS_ERR_SHAPE, "heads=%d head_dim=%d invalid", a->heads, a->head_dim);
@@ -782,6 +824,12 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   if (a->v_out && !has_v) return fail(PS_ERR_SHAPE, "v_out given without v");
   if ((norm_q || norm_k) && !(a->eps >= 0.f)) return fail(PS_ERR_SHAPE, "eps must be >= 0");
   int rc;
+  if (n_sink) {
+    if (!a->k_sink) return fail(PS_ERR_NULL, "sink sequences need k_sink");
+    if ((rc = check_ptr(a->k_sink, "k_sink")) || (rc = check_stride(a->k_sink_stride, C, es, "k_sink"))) return rc;
+    if (!a->k_out) return fail(PS_ERR_NULL, "sink sequences need k_out");
+    if (a->k_sink_rows < 0) return fail(PS_ERR_SHAPE, "k_sink_rows=%lld", (long long)a->k_sink_rows);
+  }
   if (has_q) {
     if ((rc = check_ptr(a->q, "q")) || (rc = check_stride(a->q_stride, C, es, "q")) ||
         (rc = check_ptr(a->q_out, "q_out")) || (rc = check_stride(a->q_out_stride, C, es, "q_out")))
@@ -815,9 +863,6 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
                     a->w_dim, a->head_dim);
     }
   }
-  if (a->n_seqs < 1) return fail(PS_ERR_SHAPE, "n_seqs=%d", a->n_seqs);
-  if (a->n_seqs > PS_MAX_SEQS) return fail(PS_ERR_TOO_MANY_SEQS, "n_seqs=%d exceeds PS_MAX_SEQS=%d", a->n_seqs, PS_MAX_SEQS);
-  if (!a->seqs) return fail(PS_ERR_NULL, "seqs is NULL");
   if (a->in_rows < 0) return fail(PS_ERR_SHAPE, "in_rows=%lld", (long long)a->in_rows);
   if (a->kernel != PS_KERNEL_AUTO && a->kernel != PS_KERNEL_ROWS && a->kernel != PS_KERNEL_BULK)
     return fail(PS_ERR_SHAPE, "kernel %d unknown", a->kernel);
@@ -826,7 +871,7 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   memset(&k, 0, sizeof(k));
   const bool k_out = has_k && a->k_out != nullptr;
   k.flags = (has_q ? kHasQ : 0) | (has_k ? kHasK : 0) | (has_v ? kHasV : 0) | (norm_q ? kNormQ : 0) |
-            (norm_k ? kNormK : 0) | (a->k_pre ? kKPre : 0) | (k_out ? kKOut : 0);
+            (norm_k ? kNormK : 0) | (a->k_pre ? kKPre : 0) | (k_out ? kKOut : 0) | (n_sink ? kSinkSeqs : 0);
   int64_t total = 0;
   for (int s = 0; s < a->n_seqs; ++s) {
     const ps_seq& q = a->seqs[s];
@@ -836,9 +881,11 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
     if (hw > INT32_MAX || q.n_tokens % hw)
       return fail(PS_ERR_SHAPE, "seq %d: n_tokens=%d is not whole frames of %lld tokens", s, q.n_tokens, (long long)hw);
     const int64_t frames = q.n_tokens / hw;
-    if (q.token_start < 0 || q.token_start + q.n_tokens > a->in_rows)
-      return fail(PS_ERR_BOUNDS, "seq %d: rows [%lld, %lld) outside in_rows=%lld", s, (long long)q.token_start,
-                  (long long)(q.token_start + q.n_tokens), (long long)a->in_rows);
+    const bool sink = q.kind == PS_SEQ_SINK;
+    const int64_t src_rows = sink ? a->k_sink_rows : a->in_rows;
+    if (q.token_start < 0 || q.token_start + q.n_tokens > src_rows)
+      return fail(PS_ERR_BOUNDS, "seq %d: rows [%lld, %lld) outside %s=%lld", s, (long long)q.token_start,
+                  (long long)(q.token_start + q.n_tokens), sink ? "k_sink_rows" : "in_rows", (long long)src_rows);
     if (rotate && q.n_tokens > 0) {
       if (a->table_mode == PS_TABLE_AXES) {
         if (q.frame_offset < 0 || q.frame_offset + frames > a->table_rows || q.grid_h > a->table_rows ||
@@ -874,6 +921,7 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
     d.frame_offset = q.frame_offset;
     d.ring_frames = q.ring_frames > 0 ? q.ring_frames : 1;
     d.ring_slot0 = q.ring_slot0;
+    d.kind = q.kind;
     total += q.n_tokens;
     if (total > (1 << 30)) return fail(PS_ERR_SHAPE, "more than 2^30 tokens in one call");
   }
@@ -899,6 +947,11 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   k.q = a->q; k.k = a->k; k.v = a->v; k.wq = norm_q ? a->q_weight : nullptr; k.wk = norm_k ? a->k_weight : nullptr;
   k.cos = a->cos; k.sin = a->sin;
   k.q_out = a->q_out; k.k_out = a->k_out; k.v_out = a->v_out; k.k_pre = a->k_pre;
+  k.k_sink = n_sink ? a->k_sink : nullptr;
+  k.k_sink_stride = a->k_sink_stride;
+  k.w_f32 = a->dtype == PS_BF16 && a->weight_f32 == 1;
+  k.early = a->launch == PS_LAUNCH_PDL_EARLY_INPUTS;
+  plan->launch = a->launch;
   k.q_stride = a->q_stride; k.k_stride = a->k_stride; k.v_stride = a->v_stride;
   k.q_out_stride = a->q_out_stride; k.k_out_stride = a->k_out_stride; k.v_out_stride = a->v_out_stride;
   k.k_pre_stride = a->k_pre_stride;
@@ -916,6 +969,7 @@ static int build_plan(const ps_qk_prep_args* a, Plan* plan, bool host_only) {
   k.c_f = static_cast<float>(C);
   plan->kernel = kernel;
   plan->elem_size = es;
+  if (kernel == PS_KERNEL_BULK && n_sink) return kNeedsSplit;
 
   if (kernel == PS_KERNEL_ROWS) {
     int V = a->heads_per_thread;
@@ -1043,31 +1097,54 @@ static cudaError_t allow_smem(const void* fn, int bytes) {
   return err;
 }
 
+// Launches `fn` in the call's ps_launch order (programmatic dependent launch or plain).
+static cudaError_t launch_kernel(void (*fn)(KParams), const Plan& plan, dim3 grid, dim3 block, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (plan.launch != PS_LAUNCH_STREAM) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, fn, plan.params);
+}
+
 template <typename T, int FLAGS>
-static void launch_rows(const Plan& plan, dim3 grid, dim3 block, cudaStream_t stream) {
-  switch (plan.V) {
-    case 1: rows_kernel<T, 1, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 2: rows_kernel<T, 2, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 3: rows_kernel<T, 3, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 4: rows_kernel<T, 4, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 5: rows_kernel<T, 5, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 6: rows_kernel<T, 6, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    case 8: rows_kernel<T, 8, FLAGS><<<grid, block, plan.smem, stream>>>(plan.params); break;
-    default: break;
+static void (*rows_fn(int V))(KParams) {
+  switch (V) {
+    case 1: return rows_kernel<T, 1, FLAGS>;
+    case 2: return rows_kernel<T, 2, FLAGS>;
+    case 3: return rows_kernel<T, 3, FLAGS>;
+    case 4: return rows_kernel<T, 4, FLAGS>;
+    case 5: return rows_kernel<T, 5, FLAGS>;
+    case 6: return rows_kernel<T, 6, FLAGS>;
+    case 8: return rows_kernel<T, 8, FLAGS>;
+    default: return nullptr;
   }
 }
+
+// Flag sets of the chunk prep with relocated sinks in the same launch (rows kernel).
+constexpr int kModeRingSink = kModeRing | kSinkSeqs;
 
 template <typename T>
 static cudaError_t launch_typed(const Plan& plan, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(plan.blocks)), block(plan.threads);
   if (plan.kernel == PS_KERNEL_ROWS) {
+    void (*fn)(KParams) = nullptr;
     switch (plan.params.flags) {
-      case kModeRing: launch_rows<T, kModeRing>(plan, grid, block, stream); break;
-      case kModeRef: launch_rows<T, kModeRef>(plan, grid, block, stream); break;
-      case kModeSink: launch_rows<T, kModeSink>(plan, grid, block, stream); break;
-      default: launch_rows<T, 0>(plan, grid, block, stream); break;
+      case kModeRing: fn = rows_fn<T, kModeRing>(plan.V); break;
+      case kModeRingSink: fn = rows_fn<T, kModeRingSink>(plan.V); break;
+      case kModeRef: fn = rows_fn<T, kModeRef>(plan.V); break;
+      case kModeSink: fn = rows_fn<T, kModeSink>(plan.V); break;
+      default: fn = rows_fn<T, 0>(plan.V); break;
     }
-    return cudaGetLastError();
+    if (!fn) return cudaErrorInvalidValue;
+    return launch_kernel(fn, plan, grid, block, stream);
   }
   void (*fn)(KParams) = bulk_kernel<T, 0>;
   switch (plan.params.flags) {
@@ -1078,28 +1155,88 @@ static cudaError_t launch_typed(const Plan& plan, cudaStream_t stream) {
   }
   cudaError_t err = allow_smem(reinterpret_cast<const void*>(fn), static_cast<int>(plan.smem));
   if (err != cudaSuccess) return err;
-  fn<<<grid, block, plan.smem, stream>>>(plan.params);
-  return cudaGetLastError();
+  return launch_kernel(fn, plan, grid, block, stream);
+}
+
+// The launches of one ps_qk_norm_rope_kv call: one, or two when the bulk kernel runs a call
+// with sink sequences (the chunk's sequences, then the sinks as a K-only launch).
+struct Calls {
+  Plan plan[2];
+  int n = 0;
+  std::vector<ps_seq> seqs[2];
+};
+
+// The K-only call that re-rotates the sink sequences of `a` (all of kind PS_SEQ_SINK in `sinks`).
+static ps_qk_prep_args sink_call(const ps_qk_prep_args* a, std::vector<ps_seq>& sinks) {
+  ps_qk_prep_args c = *a;
+  c.q = nullptr; c.q_weight = nullptr; c.q_out = nullptr;
+  c.v = nullptr; c.v_out = nullptr;
+  c.k_weight = nullptr; c.k_pre = nullptr;
+  c.k = a->k_sink; c.k_stride = a->k_sink_stride; c.in_rows = a->k_sink_rows;
+  c.k_sink = nullptr;
+  for (ps_seq& q : sinks) q.kind = PS_SEQ_PREP;
+  c.seqs = sinks.data();
+  c.n_seqs = static_cast<int32_t>(sinks.size());
+  return c;
+}
+
+static int plan_calls(const ps_qk_prep_args* a, Calls* calls, bool host_only) {
+  clear_error();
+  calls->n = 0;
+  if (!a) return fail(PS_ERR_NULL, "args is NULL");
+  int n_sink = 0;
+  if (a->seqs && a->n_seqs >= 1 && a->n_seqs <= PS_MAX_SEQS)
+    for (int s = 0; s < a->n_seqs; ++s) n_sink += a->seqs[s].kind == PS_SEQ_SINK;
+  if (n_sink > 0 && n_sink == a->n_seqs) {
+    // Sinks only: the specialised K-only launch reading k_sink.
+    if (!a->k_sink) return fail(PS_ERR_NULL, "sink sequences need k_sink");
+    calls->seqs[1].assign(a->seqs, a->seqs + a->n_seqs);
+    const ps_qk_prep_args c = sink_call(a, calls->seqs[1]);
+    const int rc = build_plan(&c, &calls->plan[0], host_only, false);
+    if (rc == PS_OK) calls->n = 1;
+    return rc;
+  }
+  int rc = build_plan(a, &calls->plan[0], host_only, true);
+  if (rc != kNeedsSplit) {
+    if (rc == PS_OK) calls->n = 1;
+    return rc;
+  }
+  // Bulk kernel with sink sequences: the chunk's sequences, then the sinks.
+  calls->seqs[0].clear();
+  calls->seqs[1].clear();
+  for (int s = 0; s < a->n_seqs; ++s) calls->seqs[a->seqs[s].kind == PS_SEQ_SINK ? 1 : 0].push_back(a->seqs[s]);
+  ps_qk_prep_args main_call = *a;
+  main_call.seqs = calls->seqs[0].data();
+  main_call.n_seqs = static_cast<int32_t>(calls->seqs[0].size());
+  main_call.k_sink = nullptr;
+  const ps_qk_prep_args sinks = sink_call(a, calls->seqs[1]);
+  if ((rc = build_plan(&main_call, &calls->plan[0], host_only, false)) != PS_OK) return rc;
+  if ((rc = build_plan(&sinks, &calls->plan[1], host_only, false)) != PS_OK) return rc;
+  calls->n = 2;
+  return PS_OK;
 }
 
 }  // namespace
 }  // namespace ps
 
 extern "C" int32_t ps_qk_prep_validate(const ps_qk_prep_args* args) {
-  ps::Plan plan;
-  return ps::build_plan(args, &plan, true);
+  ps::Calls calls;
+  return ps::plan_calls(args, &calls, true);
 }
 
 extern "C" int32_t ps_qk_norm_rope_kv(const ps_qk_prep_args* args, void* stream) {
-  ps::Plan plan;
-  const int rc = ps::build_plan(args, &plan, false);
+  ps::Calls calls;
+  const int rc = ps::plan_calls(args, &calls, false);
   if (rc != PS_OK) return rc;
-  if (plan.blocks == 0) return PS_OK;
-  if (plan.blocks > 0x7fffffffLL) return ps::fail(PS_ERR_UNSUPPORTED, "grid of %lld CTAs", (long long)plan.blocks);
-  const cudaError_t err = plan.elem_size == 2
-                              ? ps::launch_typed<__nv_bfloat16>(plan, static_cast<cudaStream_t>(stream))
-                              : ps::launch_typed<float>(plan, static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "qk_prep launch: %s", cudaGetErrorString(err));
+  for (int i = 0; i < calls.n; ++i) {
+    const ps::Plan& plan = calls.plan[i];
+    if (plan.blocks == 0) continue;
+    if (plan.blocks > 0x7fffffffLL) return ps::fail(PS_ERR_UNSUPPORTED, "grid of %lld CTAs", (long long)plan.blocks);
+    const cudaError_t err = plan.elem_size == 2
+                                ? ps::launch_typed<__nv_bfloat16>(plan, static_cast<cudaStream_t>(stream))
+                                : ps::launch_typed<float>(plan, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "qk_prep launch: %s", cudaGetErrorString(err));
+  }
   return PS_OK;
 }
 

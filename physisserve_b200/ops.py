@@ -114,7 +114,9 @@ class Seq:
     frame; ``frame_offset``: absolute latent frame of its first frame (per-axis tables);
     ``table_row``: table row of its first token (per-token tables); ``ring_row``,
     ``ring_frames``, ``ring_slot0``: where frame f's K/V rows go -- slot
-    (ring_slot0 + f) % ring_frames of the ring starting at row ``ring_row``.
+    (ring_slot0 + f) % ring_frames of the ring starting at row ``ring_row``; ``kind``:
+    ``SEQ_SINK`` re-rotates a relocated sink whose pre-RoPE K rows start at ``token_start``
+    of the call's ``k_sink`` (no Q, no V, no RMSNorm).
     """
 
     token_start: int
@@ -126,10 +128,11 @@ class Seq:
     ring_row: int = 0
     ring_frames: int = 0
     ring_slot0: int = 0
+    kind: int = _lib.SEQ_PREP
 
     def to_c(self) -> _lib.PsSeq:
         return _lib.PsSeq(self.token_start, self.n_tokens, self.grid_h, self.grid_w, self.frame_offset,
-                          self.table_row, self.ring_row, self.ring_frames, self.ring_slot0)
+                          self.table_row, self.ring_row, self.ring_frames, self.ring_slot0, self.kind, 0)
 
 
 def flat_seq(token_start: int, n_tokens: int, grid_h: int, grid_w: int, frame_offset: int = 0,
@@ -156,6 +159,8 @@ def varlen_seqs(cu_seqlens, grids, frame_offsets, *, ring_rows=None, ring_frames
     seqs = []
     for i in range(n):
         gh, gw = grids[i]
+        if gh < 1 or gw < 1:
+            raise PrepError(f"member {i}: grid {gh}x{gw}")
         tokens = cu[i + 1] - cu[i]
         if tokens % (gh * gw):
             raise PrepError(f"member {i}: {tokens} tokens are not whole frames of {gh}x{gw}")
@@ -205,8 +210,11 @@ def _rows(t: torch.Tensor | None, C: int, name: str):
 # ps_qk_prep_args and ps_seq packed with struct (layout checked against include/physis_b200.h
 # by the tests): building them this way costs a few microseconds per launch, which matters
 # for the small per-block launches of a single stream.
-_ARGS = struct.Struct("=8if9iq" + "Qq" * 3 + "QQQQq" + "Qq" * 3 + "q" + "Qq" + "Q")
-_SEQ = struct.Struct("=qiiiiqqii")
+_ARGS_HEAD = "=8if11iq"
+_ARGS = struct.Struct(_ARGS_HEAD + "Qq" * 3 + "QQQQq" + "Qq" * 3 + "q" + "Qq" + "Qqq" + "Q")
+_SEQ = struct.Struct("=qiiiiqqiiii")
+_LAUNCH = {"stream": _lib.LAUNCH_STREAM, "pdl": _lib.LAUNCH_PDL, "pdl_early_inputs": _lib.LAUNCH_PDL_EARLY_INPUTS}
+SEQ_PREP, SEQ_SINK = _lib.SEQ_PREP, _lib.SEQ_SINK
 _DEVICE_DTYPES = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
 
 
@@ -234,8 +242,10 @@ def _prepare(
     k_out: torch.Tensor | None = None,
     v_out: torch.Tensor | None = None,
     k_pre: torch.Tensor | None = None,
+    k_sink: torch.Tensor | None = None,
     table_mode: str = "axes",
     axis_split: Sequence[int] | None = None,
+    launch: str = "pdl",
     heads_per_thread: int = 0,
     kernel: str = "auto",
     stages: int = 0,
@@ -249,7 +259,7 @@ def _prepare(
     """Validate a ``qk_norm_rope_kv`` call and pack its ``ps_qk_prep_args`` (one buffer per
     ``PS_MAX_SEQS`` sequences); returns (device index, [(args, seq buffer)], tensor signatures)."""
     C = heads * head_dim
-    ref = q if q is not None else (k if k is not None else v)
+    ref = next((t for t in (q, k, v, k_sink) if t is not None), None)
     if ref is None:
         raise PrepError("q, k and v are all None")
     dtype = _DEVICE_DTYPES.get(ref.dtype)
@@ -259,11 +269,27 @@ def _prepare(
         raise PrepError("the prep kernels run on CUDA tensors only (there is no CPU path)")
     device_index = ref.get_device()
     for name, t in (("q", q), ("k", k), ("v", v), ("q_out", q_out), ("k_out", k_out), ("v_out", v_out),
-                    ("k_pre", k_pre), ("q_weight", q_weight), ("k_weight", k_weight)):
+                    ("k_pre", k_pre), ("k_sink", k_sink)):
         if t is not None and (t.dtype is not ref.dtype or t.get_device() != device_index):
             if not t.is_cuda:
                 raise PrepError("the prep kernels run on CUDA tensors only (there is no CPU path)")
             raise PrepError(f"{name} is {t.dtype} on {t.device}, expected {ref.dtype} on {ref.device}")
+    # RMSNorm weights: the activation dtype, or fp32 (weights kept in fp32, wan.py:146-148).
+    weights = [w for w in (q_weight, k_weight) if w is not None]
+    weight_f32 = 0
+    for name, w in (("q_weight", q_weight), ("k_weight", k_weight)):
+        if w is None:
+            continue
+        if not w.is_cuda or w.get_device() != device_index:
+            raise PrepError(f"{name} must be a CUDA tensor on {ref.device}")
+        if w.dtype is not ref.dtype and w.dtype is not torch.float32:
+            raise PrepError(f"{name} is {w.dtype}: RMSNorm weights are {ref.dtype} or float32")
+        if w.dtype is not weights[0].dtype:
+            raise PrepError("q_weight and k_weight differ in dtype")
+        weight_f32 = int(w.dtype is torch.float32)
+    launch_code = _LAUNCH.get(launch)
+    if launch_code is None:
+        raise PrepError(f"launch {launch!r} is not one of {sorted(_LAUNCH)}")
     for name, t in (("cos", cos), ("sin", sin)):
         if t.dtype is not torch.float32:
             raise PrepError(f"{name} must be float32")
@@ -291,8 +317,9 @@ def _prepare(
     kop, kos, ko_rows = _rows(k_out, C, "k_out")
     vop, vos, vo_rows = _rows(v_out, C, "v_out")
     kpp, kps, kp_rows = _rows(k_pre, C, "k_pre")
-    in_rows = min(r for r, t in ((q_rows, q), (k_rows, k), (v_rows, v), (qo_rows, q_out), (kp_rows, k_pre))
-                  if t is not None)
+    ksp, kss, ks_rows = _rows(k_sink, C, "k_sink")
+    in_rows = min([r for r, t in ((q_rows, q), (k_rows, k), (v_rows, v), (qo_rows, q_out), (kp_rows, k_pre))
+                   if t is not None] or [0])
     kv_rows = min([r for r, t in ((ko_rows, k_out), (vo_rows, v_out)) if t is not None] or [0])
     table_rows = cos.numel() // head_dim
     kern = _KERNELS.get(kernel)
@@ -308,16 +335,17 @@ def _prepare(
         seq_buf = ctypes.create_string_buffer(_SEQ.size * max(1, len(part)))
         for i, sq in enumerate(part):
             _SEQ.pack_into(seq_buf, i * _SEQ.size, sq.token_start, sq.n_tokens, sq.grid_h, sq.grid_w,
-                           sq.frame_offset, sq.table_row, sq.ring_row, sq.ring_frames, sq.ring_slot0)
+                           sq.frame_offset, sq.table_row, sq.ring_row, sq.ring_frames, sq.ring_slot0, sq.kind, 0)
         args = ctypes.create_string_buffer(_ARGS.size)
         _ARGS.pack_into(args, 0, dtype, heads, head_dim, mode, split[0], split[1], split[2], len(part), float(eps),
                         heads_per_thread, kern, stages, groups, ctas_per_sm, row_threads, release, vstages, vdepth,
+                        weight_f32, launch_code,
                         in_rows, qp or 0, qs, kp or 0, ks, vp or 0, vs, qw, kw, cos.data_ptr(), sin.data_ptr(),
                         table_rows, qop or 0, qos, kop or 0, kos, vop or 0, vos, kv_rows, kpp or 0, kps,
-                        ctypes.addressof(seq_buf))
+                        ksp or 0, kss, ks_rows, ctypes.addressof(seq_buf))
         parts.append((args, seq_buf))
     signatures = {name: _signature(t) for name, t in (("q", q), ("k", k), ("v", v), ("q_weight", q_weight),
-                                                      ("k_weight", k_weight))}
+                                                      ("k_weight", k_weight), ("q_out", q_out))}
     return device_index, parts, signatures
 
 
@@ -325,7 +353,14 @@ def _signature(t: torch.Tensor | None):
     return None if t is None else (t.shape, t.stride(), t.dtype, t.device)
 
 
-def qk_norm_rope_kv(**kwargs) -> None:
+def _raise_on_timeouts(device_index: int) -> None:
+    count = device_timeouts(reset=True, device=device_index)
+    if count:
+        raise PrepError(f"{count} bounded wait(s) of the bulk kernel ran out on cuda:{device_index}: "
+                        "the outputs of the launches since the last check are undefined")
+
+
+def qk_norm_rope_kv(*, check_timeouts: bool = False, **kwargs) -> None:
     """One fused launch (per ``PS_MAX_SEQS`` sequences) of ``ps_qk_norm_rope_kv``.
 
     Replaces norm_q/norm_k (wan.py:104-105), the K/V write of ``Cache`` (kv_cache.py:51-56)
@@ -335,10 +370,18 @@ def qk_norm_rope_kv(**kwargs) -> None:
     ``table_mode`` -- "axes" (``cos``/``sin`` are the [max_len, D] per-axis tables, positions
     decoded from each sequence's grid and frame offset) or "tokens" (``cos``/``sin`` are
     per-token rows, [rows, D] or the reference's [B, L, 1, D] tables, read at
-    ``table_row + l``) -- ``axis_split``, and the tiling knobs ``kernel`` ("auto", "bulk" =
-    persistent cp.async.bulk pipeline, "rows"), ``heads_per_thread`` (rows), ``row_threads``,
-    ``stages``, ``groups``, ``ctas_per_sm``, ``release``, ``vstages``, ``vdepth`` (bulk), all
-    defaulting to the library's choice.
+    ``table_row + l``) -- ``axis_split``, ``k_sink`` (pre-RoPE K rows of ``SEQ_SINK``
+    sequences), ``launch`` ("pdl" (default): programmatic dependent launch that waits for the
+    previous kernel before touching memory; "stream"; "pdl_early_inputs": inputs read before
+    that wait, only for inputs no running kernel writes), and the tiling knobs ``kernel``
+    ("auto", "bulk" = persistent cp.async.bulk pipeline, "rows"), ``heads_per_thread`` (rows),
+    ``row_threads``, ``stages``, ``groups``, ``ctas_per_sm``, ``release``, ``vstages``,
+    ``vdepth`` (bulk), all defaulting to the library's choice.  ``q_weight``/``k_weight``
+    may be float32 with bfloat16 activations (weights kept in fp32).
+
+    ``check_timeouts=True`` synchronises the device after the launch and raises ``PrepError``
+    if a bounded wait of the bulk kernel ran out since the last check (the outputs are then
+    undefined); without it, callers poll ``device_timeouts``.
     """
     device_index, parts, _ = _prepare(**kwargs)
     lib = _lib.load()
@@ -346,18 +389,24 @@ def qk_norm_rope_kv(**kwargs) -> None:
         stream = _current_stream(device_index)
         for args, _seq_buf in parts:
             _check(lib.ps_qk_norm_rope_kv(args, stream))
+    if check_timeouts:
+        _raise_on_timeouts(device_index)
 
 
-qk_norm_rope_kv.__signature__ = inspect.signature(_prepare).replace(return_annotation=None)
+qk_norm_rope_kv.__signature__ = inspect.signature(_prepare).replace(
+    parameters=[inspect.Parameter("check_timeouts", inspect.Parameter.KEYWORD_ONLY, default=False),
+                *inspect.signature(_prepare).parameters.values()],
+    return_annotation=None)
 
 
 # Byte offsets of the pointer fields a plan swaps between launches.
 _FIELD_OFFSETS = {
-    "q": struct.calcsize("=8if9iq"),
-    "k": struct.calcsize("=8if9iq" + "Qq"),
-    "v": struct.calcsize("=8if9iq" + "Qq" * 2),
-    "q_weight": struct.calcsize("=8if9iq" + "Qq" * 3),
-    "k_weight": struct.calcsize("=8if9iq" + "Qq" * 3 + "Q"),
+    "q": struct.calcsize(_ARGS_HEAD),
+    "k": struct.calcsize(_ARGS_HEAD + "Qq"),
+    "v": struct.calcsize(_ARGS_HEAD + "Qq" * 2),
+    "q_weight": struct.calcsize(_ARGS_HEAD + "Qq" * 3),
+    "k_weight": struct.calcsize(_ARGS_HEAD + "Qq" * 3 + "Q"),
+    "q_out": struct.calcsize(_ARGS_HEAD + "Qq" * 3 + "QQQQq"),
 }
 
 
@@ -366,7 +415,7 @@ class PrepPlan:
 
     The per-block loop of a serving step (30 blocks x 4 denoising steps of the same streams)
     repeats one call shape with new activations and per-block norm weights.  ``launch`` swaps
-    the q/k/v/weight pointers into the packed ``ps_qk_prep_args`` and calls the library; each
+    the q/k/v/weight/q_out pointers into the packed ``ps_qk_prep_args`` and calls the library; each
     swapped tensor must have the planned shape, strides, dtype and device (checked), and the
     library re-validates every launch on the host.  Sequences, tables and outputs are fixed.
     """
@@ -375,11 +424,13 @@ class PrepPlan:
         self.device_index, self.parts, self.signatures = _prepare(**kwargs)
         self._lib = _lib.load()
 
-    def launch(self, **tensors) -> None:
+    def launch(self, *, check_timeouts: bool = False, **tensors) -> None:
+        """One launch with the given tensors swapped in.  ``check_timeouts=True`` (for the end
+        of a serving step) synchronises and raises ``PrepError`` if a bounded wait ran out."""
         for name, t in tensors.items():
             want = self.signatures.get(name, False)
             if want is False:
-                raise PrepError(f"{name} cannot be swapped in a plan (only q, k, v, q_weight, k_weight)")
+                raise PrepError(f"{name} cannot be swapped in a plan (only q, k, v, q_weight, k_weight, q_out)")
             if want is None or t is None or (t.shape, t.stride(), t.dtype, t.device) != want:
                 raise PrepError(f"{name} must match the planned tensor (shape, strides, dtype, device)")
             ptr = t.data_ptr()
@@ -389,6 +440,8 @@ class PrepPlan:
             stream = _current_stream(self.device_index)
             for args, _seq_buf in self.parts:
                 _check(self._lib.ps_qk_norm_rope_kv(args, stream))
+        if check_timeouts:
+            _raise_on_timeouts(self.device_index)
 
 
 _KERNELS = {"auto": _lib.KERNEL_AUTO, "rows": _lib.KERNEL_ROWS, "bulk": _lib.KERNEL_BULK}
@@ -556,10 +609,14 @@ def wait_selftest(limit_us: int = 20000, device: int | None = None) -> None:
         _check(_lib.load().ps_wait_selftest(int(limit_us), _current_stream(index)))
 
 
-def device_timeouts(reset: bool = True) -> int:
-    """Bounded waits of the bulk kernel that ran out on the current device (synchronises)."""
+def device_timeouts(reset: bool = True, device: int | None = None) -> int:
+    """Bounded waits of the bulk kernel that ran out on ``device`` (default: the current
+    device) since the last reset; synchronises that device.  A non-zero count means the
+    outputs of the launches since then are undefined."""
+    index = torch.cuda.current_device() if device is None else int(device)
     count = ctypes.c_uint32(0)
-    _check(_lib.load().ps_device_timeouts(ctypes.byref(count), int(reset)))
+    with _on_device(index):
+        _check(_lib.load().ps_device_timeouts(ctypes.byref(count), int(reset)))
     return int(count.value)
 
 

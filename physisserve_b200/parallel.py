@@ -13,6 +13,7 @@ history of its own blocks, so no KV ever moves (model_runner.py:44-69).
 from __future__ import annotations
 
 import datetime
+import math
 from dataclasses import dataclass
 from typing import Callable, Sequence
 
@@ -92,6 +93,144 @@ def _exchange(send=None, recv=None, group=None):
         ops.append(dist.P2POp(dist.irecv, recv[0], recv[1], group=group))
     for work in dist.batch_isend_irecv(ops):
         work.wait()
+
+
+# --------------------------------------------------------------------------------------
+# Asynchronous stage handoff
+# --------------------------------------------------------------------------------------
+class _Handle:
+    """One backend work handle shared by every consumer of a posted batch: the backend is
+    waited on at most once (gloo receive handles allow one wait), while completion for
+    buffer retention is polled separately (a stream wait does not mean the copy is done)."""
+
+    __slots__ = ("work", "waited")
+
+    def __init__(self, work):
+        self.work, self.waited = work, False
+
+    def wait(self):
+        if not self.waited:
+            self.work.wait()
+            self.waited = True
+
+    def done(self) -> bool:
+        return bool(self.work.is_completed())
+
+
+class Pending:
+    """The tensors of one received item.  ``wait()`` returns them once they hold the data:
+    for NCCL it makes the current CUDA stream wait (the host goes on), for gloo it blocks.
+    The consumer waits when it runs, not when the transfer is posted (transport.py:54-67,
+    model_runner.py:184)."""
+
+    __slots__ = ("tensors", "handles")
+
+    def __init__(self, tensors, handles=()):
+        self.tensors, self.handles = tensors, tuple(handles)
+
+    def wait(self):
+        for h in self.handles:
+            h.wait()
+        self.handles = ()
+        return self.tensors
+
+
+def _dtype_groups(spec):
+    """Indices of ``spec`` entries grouped by dtype, in first-appearance order."""
+    groups = {}
+    for i, (_, dtype) in enumerate(spec):
+        groups.setdefault(dtype, []).append(i)
+    return list(groups.items())
+
+
+class Transport:
+    """Ordered point-to-point transfers between the ranks of a stage pipeline, posted
+    asynchronously (the contract of the reference's ``Distributed`` transport,
+    engine/transport.py:84-156).
+
+    ``transfer(items)`` takes ``(tag, src, dst, spec, tensors)`` items in the same order on
+    every rank; ``spec`` is ``[(shape, dtype), ...]`` and ``tensors`` is needed on the source
+    only.  All of a call's sends and receives go out as one ``batch_isend_irecv``; the result
+    maps the tags this rank receives (or keeps, when src == dst) to ``Pending``.
+
+    Same-dtype tensors of an item travel as ONE message: the sender copies them into one
+    contiguous packet, the receiver receives into one allocation and hands out views of it
+    (a hidden state and a latent are one message, not two).  Receive allocations are fresh
+    per transfer, never pooled, because callers keep received tensors.  Every posted packet
+    and receive buffer stays referenced until the backend reports the operation complete,
+    so callers may drop or overwrite their own tensors as soon as ``transfer`` returns.
+    """
+
+    def __init__(self, device, group=None):
+        self.device, self.group = torch.device(device), group
+        self.rank = dist.get_rank(group)
+        self.inflight = []  # (handles, tensors) kept until every handle reports completion
+
+    def _peer(self, rank: int) -> int:
+        return dist.get_global_rank(self.group, rank) if self.group is not None else rank
+
+    def _receive_packets(self, spec):
+        """(views in spec order, packet buffers) for one received item."""
+        views = [None] * len(spec)
+        packets = []
+        for dtype, idx in _dtype_groups(spec):
+            sizes = [math.prod(spec[i][0]) for i in idx]
+            packet = torch.empty(sum(sizes), dtype=dtype, device=self.device)
+            offset = 0
+            for i, n in zip(idx, sizes):
+                views[i] = packet.narrow(0, offset, n).view(spec[i][0])
+                offset += n
+            packets.append(packet)
+        return tuple(views), packets
+
+    def _send_packets(self, spec, tensors):
+        packets = []
+        for dtype, idx in _dtype_groups(spec):
+            parts = [tensors[i] for i in idx]
+            for i in idx:
+                if tuple(tensors[i].shape) != tuple(spec[i][0]) or tensors[i].dtype != dtype:
+                    raise ValueError(f"tensor {i} is {tuple(tensors[i].shape)} {tensors[i].dtype}, spec says "
+                                     f"{tuple(spec[i][0])} {dtype}")
+            if len(parts) == 1:
+                packets.append(parts[0].reshape(-1).contiguous())
+            else:
+                packets.append(torch.cat([t.reshape(-1) for t in parts]))
+        return packets
+
+    def transfer(self, items):
+        self.inflight = [entry for entry in self.inflight if not all(h.done() for h in entry[0])]
+        ops, kept, received, result = [], [], {}, {}
+        for tag, src, dst, spec, tensors in items:
+            if src == dst:
+                if src == self.rank:
+                    result[tag] = Pending(tensors)
+                continue
+            if dst == self.rank:
+                views, packets = self._receive_packets(spec)
+                received[tag] = (views, len(ops), len(ops) + len(packets))
+                ops += [dist.P2POp(dist.irecv, b, self._peer(src), group=self.group) for b in packets]
+                kept += packets
+            elif src == self.rank:
+                packets = self._send_packets(spec, tensors)
+                ops += [dist.P2POp(dist.isend, b, self._peer(dst), group=self.group) for b in packets]
+                kept += packets
+        if not ops:
+            return result
+        handles = [_Handle(w) for w in dist.batch_isend_irecv(ops)]
+        self.inflight.append((handles, tuple(kept)))
+        # Gloo gives one handle per operation; coalesced NCCL may give one for the whole batch,
+        # which every receiver then shares.
+        per_op = len(handles) == len(ops)
+        for tag, (views, first, last) in received.items():
+            result[tag] = Pending(views, handles[first:last] if per_op else handles)
+        return result
+
+    def flush(self):
+        """Wait for everything still in flight (the end of a request)."""
+        for handles, _ in self.inflight:
+            for h in handles:
+                h.wait()
+        self.inflight = []
 
 
 def init_process_group(backend: str, timeout_s: float = 60.0, device_id=None):

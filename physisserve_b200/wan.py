@@ -27,7 +27,7 @@ from typing import Sequence
 import torch
 import torch.nn.functional as F
 
-from .ops import PrepError, Seq, _default_split, flat_seq, qk_norm_rope_kv, ring_slot, rope
+from .ops import SEQ_SINK, PrepError, Seq, _default_split, flat_seq, qk_norm_rope_kv, ring_slot, rope
 
 ATTENTION_SINK_CHUNKS = 1   # engine/kv_cache.py:28
 HISTORY_CHUNKS = 18         # engine/kv_cache.py:29
@@ -61,10 +61,13 @@ def wan_rope_tables(head_dim: int, max_len: int, theta: float = 10000.0, device=
 # Reference layout: drop-in processor
 # --------------------------------------------------------------------------------------
 def _norm_weight(module, C, dtype, device):
+    """The RMSNorm module's weight: of the activation dtype, or fp32 when the model keeps it in
+    fp32 (``_keep_in_fp32_modules``, wan.py:146-148); the output stays in the activation dtype,
+    as torch.nn.RMSNorm's does for a bf16 input and an fp32 weight."""
     weight = getattr(module, "weight", None)
     if weight is None:
         return torch.ones(C, dtype=dtype, device=device)  # (x*r)*1 == x*r exactly
-    if weight.dtype != dtype:
+    if weight.dtype != dtype and weight.dtype != torch.float32:
         raise PrepError(f"RMSNorm weight is {weight.dtype} but activations are {dtype}")
     return weight.contiguous()
 
@@ -246,6 +249,11 @@ def prep_ring(q, k, v, q_weight, k_weight, eps, freqs_cos, freqs_sin, cache: Rin
     for b, pos in enumerate(positions):
         if pos.frames * hw != L:
             raise PrepError(f"member {b}: {pos.frames} frames of {hw} tokens != {L}")
+        if pos.chunk >= 1 and pos.frames != 1:
+            # The ring holds one one-frame chunk per slot (window_rows counts chunks); a longer
+            # later chunk would overwrite the next chunk's slot.
+            raise PrepError(f"member {b}: chunk {pos.chunk} has {pos.frames} frames; the ring layout holds "
+                            "one-frame chunks after the first")
         if pos.chunk == 0:
             seqs.append(Seq(b * L, L, cache.grid_h, cache.grid_w, frame_offset=pos.frame_offset,
                             ring_row=b * rows, ring_frames=cache.sink_frames, ring_slot0=0))
@@ -259,24 +267,22 @@ def prep_ring(q, k, v, q_weight, k_weight, eps, freqs_cos, freqs_sin, cache: Rin
         if not all(p.chunk == 0 for p in positions):
             raise PrepError("a first chunk is batched only with other first chunks (its own schedule)")
         k_pre = cache.sink_k.view(-1, C)
+    # The sink region must hold the sink rotated at this call's window position; chunk 0
+    # wrote it at frame 0.  Wherever the position moved, the pre-RoPE sink is re-rotated by
+    # sink sequences of the same launch.
+    moved = [(b, p.sink_position) for b, p in enumerate(positions)
+             if p.chunk != 0 and cache.sink_at[b] != p.sink_position]
+    seqs += [Seq(b * cache.sink_rows, cache.sink_rows, cache.grid_h, cache.grid_w, frame_offset=at,
+                 ring_row=b * rows, ring_frames=cache.sink_frames, ring_slot0=0, kind=SEQ_SINK) for b, at in moved]
     qk_norm_rope_kv(heads=cache.heads, head_dim=cache.head_dim, seqs=seqs, cos=freqs_cos, sin=freqs_sin, q=q, k=k,
                     v=v, q_weight=q_weight, k_weight=k_weight, eps=eps, q_out=q_out, k_out=pool_k, v_out=pool_v,
-                    k_pre=k_pre, table_mode="axes", axis_split=axis_split, heads_per_thread=heads_per_thread)
-    # The sink region must hold the sink rotated at this call's window position; chunk 0
-    # wrote it at frame 0.  Re-rotate the pre-RoPE sink wherever the position moved.
-    moved = []
+                    k_pre=k_pre, k_sink=cache.sink_k.view(-1, C) if moved else None, table_mode="axes",
+                    axis_split=axis_split, heads_per_thread=heads_per_thread)
     for b, p in enumerate(positions):
         if p.chunk == 0:
             cache.sink_at[b] = 0
-        elif cache.sink_at[b] != p.sink_position:
-            moved.append((b, p.sink_position))
-    if moved:
-        sink_seqs = [Seq(b * cache.sink_rows, cache.sink_rows, cache.grid_h, cache.grid_w, frame_offset=at,
-                         ring_row=b * rows, ring_frames=cache.sink_frames, ring_slot0=0) for b, at in moved]
-        qk_norm_rope_kv(heads=cache.heads, head_dim=cache.head_dim, seqs=sink_seqs, cos=freqs_cos, sin=freqs_sin,
-                        k=cache.sink_k.view(-1, C), k_out=pool_k, table_mode="axes", axis_split=axis_split)
-        for b, at in moved:
-            cache.sink_at[b] = at
+    for b, at in moved:
+        cache.sink_at[b] = at
     return q_out
 
 

@@ -61,7 +61,7 @@ static int validate_mode(void) {
   expect(ps_abi_version() == PS_ABI_VERSION, "ABI version");
   /* fake, 16-byte aligned addresses: validation never dereferences them */
   char* base = (char*)(uintptr_t)(1ull << 40);
-  ps_seq seq = {0, T, GH, GW, OFFSET, 0, 0, CAP, OFFSET % CAP};
+  ps_seq seq = {0, T, GH, GW, OFFSET, 0, 0, CAP, OFFSET % CAP, PS_SEQ_PREP, 0};
   ps_qk_prep_args a;
   fill_args(&a, &seq);
   a.q = base; a.k = base + 0x100000; a.v = base + 0x200000;
@@ -153,7 +153,7 @@ static int run_mode(void) {
   CHECK_CUDA(cudaMemset(dring_v, 0, CAP * T * row_bytes));
 
   const int slot = OFFSET % CAP;
-  ps_seq seq = {0, T, GH, GW, OFFSET, 0, 0, CAP, slot};
+  ps_seq seq = {0, T, GH, GW, OFFSET, 0, 0, CAP, slot, PS_SEQ_PREP, 0};
   ps_qk_prep_args a;
   fill_args(&a, &seq);
   a.q = dq; a.k = dk; a.v = dv; a.q_weight = dwq; a.k_weight = dwk;

@@ -53,17 +53,24 @@ int main(void) {
          sizeof(ps_qk_prep_args), offsetof(ps_qk_prep_args, seqs));
   printf("%zu %zu %zu\\n", offsetof(ps_qk_prep_args, in_rows), offsetof(ps_qk_prep_args, cos),
          offsetof(ps_qk_prep_args, k_pre_stride));
+  printf("%zu %zu %zu %zu %zu\\n", offsetof(ps_seq, kind), offsetof(ps_qk_prep_args, weight_f32),
+         offsetof(ps_qk_prep_args, launch), offsetof(ps_qk_prep_args, k_sink),
+         offsetof(ps_qk_prep_args, k_sink_rows));
   return 0;
 }
 """)
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", str(INCLUDE), str(src), "-o", str(exe)], check=True)
-    line1, line2 = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")[:2]
+    line1, line2, line3 = subprocess.run([str(exe)], capture_output=True, text=True,
+                                         check=True).stdout.split("\n")[:3]
     want1 = [ctypes.sizeof(_lib.PsSeq), _lib.PsSeq.table_row.offset, _lib.PsSeq.ring_slot0.offset,
              ctypes.sizeof(_lib.PsQkPrepArgs), _lib.PsQkPrepArgs.seqs.offset]
     want2 = [_lib.PsQkPrepArgs.in_rows.offset, _lib.PsQkPrepArgs.cos.offset, _lib.PsQkPrepArgs.k_pre_stride.offset]
+    want3 = [_lib.PsSeq.kind.offset, _lib.PsQkPrepArgs.weight_f32.offset, _lib.PsQkPrepArgs.launch.offset,
+             _lib.PsQkPrepArgs.k_sink.offset, _lib.PsQkPrepArgs.k_sink_rows.offset]
     assert [int(x) for x in line1.split()] == want1
     assert [int(x) for x in line2.split()] == want2
+    assert [int(x) for x in line3.split()] == want3
 
 
 # ---------------------------------------------------------------------------------------
@@ -144,6 +151,45 @@ def test_validate_rejects_sequences(lib, seq, text):
     assert text in message
 
 
+@pytest.mark.parametrize("over,status,text", [
+    (dict(weight_f32=2), _lib.ERR_DTYPE, "weight_f32"),
+    (dict(launch=3), _lib.ERR_SHAPE, "launch mode 3"),
+])
+def test_validate_rejects_new_fields(lib, over, status, text):
+    got, message = _validate(lib, _args(**over))
+    assert got == status, message
+    assert text in message
+
+
+@pytest.mark.parametrize("over", [dict(weight_f32=1), dict(launch=_lib.LAUNCH_PDL),
+                                  dict(launch=_lib.LAUNCH_PDL_EARLY_INPUTS)])
+def test_validate_accepts_fp32_weights_and_launch_modes(lib, over):
+    assert _validate(lib, _args(**over)) == (_lib.OK, "")
+
+
+def _sink_seq(start=0, position=7, ring_row=0):
+    return _lib.PsSeq(start, 3 * 1560, 30, 52, position, 0, ring_row, 3, 0, _lib.SEQ_SINK, 0)
+
+
+def test_validate_sink_sequences(lib):
+    """A chunk and a relocated sink in one call (rows kernel); the bulk kernel splits the call."""
+    chunk = _lib.PsSeq(0, 1560, 30, 52, 30, 0, 3 * 1560, 12, 3)
+    sink = dict(k_sink=BASE + 0x80000000, k_sink_stride=1536, k_sink_rows=3 * 1560)
+    kv = dict(kv_out_rows=15 * 1560)
+    assert _validate(lib, _args(seqs=[chunk, _sink_seq()], **sink, **kv)) == (_lib.OK, "")
+    assert _validate(lib, _args(seqs=[chunk, _sink_seq()], kernel=_lib.KERNEL_BULK, **sink, **kv))[0] == _lib.OK
+    # sinks only: a K-only call that reads k_sink
+    assert _validate(lib, _args(seqs=[_sink_seq()], q=None, q_weight=None, q_out=None, v=None, v_out=None, k=None,
+                                k_weight=None, **sink, **kv)) == (_lib.OK, "")
+    got, message = _validate(lib, _args(seqs=[chunk, _sink_seq()], **kv))
+    assert got == _lib.ERR_NULL and "k_sink" in message
+    got, message = _validate(lib, _args(seqs=[chunk, _sink_seq(start=1)], **sink, **kv))
+    assert got == _lib.ERR_BOUNDS and "k_sink_rows" in message
+    bad = _lib.PsSeq(0, 1560, 30, 52, 30, 0, 3 * 1560, 12, 3, 5, 0)
+    got, message = _validate(lib, _args(seqs=[bad], **kv))
+    assert got == _lib.ERR_SHAPE and "kind 5" in message
+
+
 def test_validate_too_many_sequences(lib):
     seqs = [_lib.PsSeq(0, 0, 1, 1, 0, 0, 0, 1, 0)] * (_lib.MAX_SEQS + 1)
     got, message = _validate(lib, _args(seqs=seqs))
@@ -176,23 +222,24 @@ def test_packed_arguments_match_the_header_layout():
     the header (whose offsets test_struct_layout_matches_header checks against the C compiler)."""
     from physisserve_b200 import ops
 
-    values = [3, 40, 128, 1, 44, 42, 42, 8, 1e-6, 5, 2, 7, 6, 1, 64, 3, 4, 2, 12480]
+    values = [3, 40, 128, 1, 44, 42, 42, 8, 1e-6, 5, 2, 7, 6, 1, 64, 3, 4, 2, 1, 2, 12480]
     ptrs = [(1 << 40) + 16 * i for i in range(30)]
     args = _lib.PsQkPrepArgs(
         dtype=3, heads=40, head_dim=128, table_mode=1, t_dim=44, h_dim=42, w_dim=42, n_seqs=8, eps=1e-6,
         heads_per_thread=5, kernel=2, stages=7, groups=6, ctas_per_sm=1, row_threads=64, release=3, vstages=4,
-        vdepth=2, in_rows=12480, q=ptrs[0], q_stride=5120, k=ptrs[1], k_stride=5121, v=ptrs[2], v_stride=5122,
-        q_weight=ptrs[3], k_weight=ptrs[4], cos=ptrs[5], sin=ptrs[6], table_rows=4096, q_out=ptrs[7],
-        q_out_stride=5123, k_out=ptrs[8], k_out_stride=5124, v_out=ptrs[9], v_out_stride=5125, kv_out_rows=99,
-        k_pre=ptrs[10], k_pre_stride=5126)
+        vdepth=2, weight_f32=1, launch=2, in_rows=12480, q=ptrs[0], q_stride=5120, k=ptrs[1], k_stride=5121,
+        v=ptrs[2], v_stride=5122, q_weight=ptrs[3], k_weight=ptrs[4], cos=ptrs[5], sin=ptrs[6], table_rows=4096,
+        q_out=ptrs[7], q_out_stride=5123, k_out=ptrs[8], k_out_stride=5124, v_out=ptrs[9], v_out_stride=5125,
+        kv_out_rows=99, k_pre=ptrs[10], k_pre_stride=5126, k_sink=ptrs[12], k_sink_stride=5127, k_sink_rows=77)
     args.seqs = ctypes.cast(ctypes.c_void_p(ptrs[11]), ctypes.POINTER(_lib.PsSeq))
     packed = ops._ARGS.pack(*values, ptrs[0], 5120, ptrs[1], 5121, ptrs[2], 5122, ptrs[3], ptrs[4], ptrs[5], ptrs[6],
-                            4096, ptrs[7], 5123, ptrs[8], 5124, ptrs[9], 5125, 99, ptrs[10], 5126, ptrs[11])
+                            4096, ptrs[7], 5123, ptrs[8], 5124, ptrs[9], 5125, 99, ptrs[10], 5126, ptrs[12], 5127, 77,
+                            ptrs[11])
     assert ops._ARGS.size == ctypes.sizeof(_lib.PsQkPrepArgs)
     assert packed == bytes(args)
-    seq = _lib.PsSeq(7, 1560, 30, 52, 9, 11, 13, 12, 5)
+    seq = _lib.PsSeq(7, 1560, 30, 52, 9, 11, 13, 12, 5, 1, 0)
     assert ops._SEQ.size == ctypes.sizeof(_lib.PsSeq)
-    assert ops._SEQ.pack(7, 1560, 30, 52, 9, 11, 13, 12, 5) == bytes(seq)
+    assert ops._SEQ.pack(7, 1560, 30, 52, 9, 11, 13, 12, 5, 1, 0) == bytes(seq)
 
 
 def test_plan_pointer_offsets_match_header():
@@ -202,7 +249,8 @@ def test_plan_pointer_offsets_match_header():
 
     A = _lib.PsQkPrepArgs
     assert ops._FIELD_OFFSETS == {"q": A.q.offset, "k": A.k.offset, "v": A.v.offset,
-                                  "q_weight": A.q_weight.offset, "k_weight": A.k_weight.offset}
+                                  "q_weight": A.q_weight.offset, "k_weight": A.k_weight.offset,
+                                  "q_out": A.q_out.offset}
 
 
 @pytest.mark.parametrize("shape,strides,rows,row_stride", [

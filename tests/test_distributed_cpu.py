@@ -11,8 +11,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from physisserve_b200.parallel import (PipelineLayout, max_over_ranks, pipeline_tick, shard_streams, stage_blocks,
-                                       sum_over_ranks)
+from physisserve_b200 import parallel
+from physisserve_b200.parallel import (PipelineLayout, Transport, max_over_ranks, pipeline_tick, shard_streams,
+                                       stage_blocks, sum_over_ranks)
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -61,6 +62,31 @@ def _worker(rank, world, port, scenario, result_dir):
                 hidden = pipeline_tick(layout, rank, hidden, lambda x: x * 2 + (rank + 1))
                 trace.append(float(hidden[0, 0]))
             out["trace"] = trace
+        elif scenario == "transport":
+            # Two lanes per rank, exchanged every iteration in both directions; each rank drops
+            # its own tensors right after posting (the transport must keep them alive).
+            bus = Transport("cpu")
+            peer = 1 - rank
+            spec = [((3, 4), torch.float32), ((5,), torch.float32), ((2,), torch.int64)]
+            lanes = [None, None]
+            seen = []
+            for it in range(6):
+                for lane in range(2):
+                    if lanes[lane] is not None:
+                        hidden, small, idx = lanes[lane].wait()
+                        seen.append((it, lane, float(hidden[0, 0]), float(small[0]), int(idx[1]),
+                                     hidden.untyped_storage().data_ptr() == small.untyped_storage().data_ptr()))
+                    mine = (torch.full((3, 4), 100.0 * rank + 10 * it + lane), torch.full((5,), float(it)),
+                            torch.tensor([rank, it]))
+                    items = [("x", rank, peer, spec, mine), ("y", peer, rank, spec, None)]
+                    got = bus.transfer(items if rank == 0 else items[::-1])
+                    del mine
+                    lanes[lane] = got["y"]
+            for lane in range(2):
+                lanes[lane].wait()
+            bus.flush()
+            out["seen"] = seen
+            out["inflight"] = len(bus.inflight)
         elif scenario == "reduce":
             out["max"] = max_over_ranks(rank * 3.5 + 1)
             out["sum"] = sum_over_ranks([rank, 1.0])
@@ -112,6 +138,96 @@ def test_pipeline_ring_handoff_gloo(tmp_path):
     # rank 0 receives from rank 1 each tick; rank 1 from rank 0.
     assert res[0]["trace"] == [f1(mb1), f1(f0(mb0)), f1(f0(f1(mb1))), f1(f0(f1(f0(mb0))))]
     assert res[1]["trace"] == [f0(mb0), f0(f1(mb1)), f0(f1(f0(mb0))), f0(f1(f0(f1(mb1))))]
+
+
+def test_transport_lanes_gloo(tmp_path):
+    """Asynchronous handoff of two lanes between two ranks over gloo: every received item holds
+    what the peer sent in the same (iteration, lane), same-dtype tensors arrive as views of one
+    packet, and nothing is left in flight after flush."""
+    res = _run("transport", tmp_path)
+    for rank in (0, 1):
+        peer = 1 - rank
+        want = [(it, lane, 100.0 * peer + 10 * (it - 1) + lane, float(it - 1), it - 1, True)
+                for it in range(1, 6) for lane in range(2)]
+        assert res[rank]["seen"] == want
+        assert res[rank]["inflight"] == 0
+
+
+class _FakeWork:
+    def __init__(self, log, index):
+        self.log, self.index, self.complete, self.waits = log, index, False, 0
+
+    def wait(self):
+        self.waits += 1
+        assert self.waits == 1, "a backend handle was waited twice"
+        self.log.append(self.index)
+
+    def is_completed(self):
+        return self.complete
+
+
+@pytest.fixture
+def fake_dist(monkeypatch):
+    posted, works, waits = [], [], []
+
+    def batch(ops):
+        posted.append([(op.op.__name__, op.peer, tuple(op.tensor.shape), op.tensor.dtype) for op in ops])
+        made = [_FakeWork(waits, len(works) + i) for i in range(len(ops))]
+        works.extend(made)
+        return made
+
+    class Op:
+        def __init__(self, op, tensor, peer, group=None):
+            self.op, self.tensor, self.peer = op, tensor, peer
+
+    monkeypatch.setattr(parallel.dist, "get_rank", lambda group=None: 0)
+    monkeypatch.setattr(parallel.dist, "P2POp", Op)
+    monkeypatch.setattr(parallel.dist, "batch_isend_irecv", batch)
+    return posted, works, waits
+
+
+def test_transport_coalesces_same_dtype_tensors_and_retains_buffers(fake_dist):
+    posted, works, waits = fake_dist
+    bus = Transport("cpu")
+    spec = [((2, 3), torch.float32), ((4,), torch.float32), ((2,), torch.int64)]
+    send = (torch.ones(2, 3), torch.full((4,), 2.0), torch.tensor([7, 8]))
+    got = bus.transfer([("out", 0, 1, spec, send), ("in", 2, 0, spec, None), ("keep", 0, 0, spec, send)])
+    # one message per dtype and item, in item order: the float32 packet holds 6 + 4 elements
+    names = [(name, peer, shape, dtype) for name, peer, shape, dtype in posted[0]]
+    assert names == [("isend", 1, (10,), torch.float32), ("isend", 1, (2,), torch.int64),
+                     ("irecv", 2, (10,), torch.float32), ("irecv", 2, (2,), torch.int64)]
+    assert set(got) == {"in", "keep"} and got["keep"].wait() is send
+    a, b, c = got["in"].tensors
+    assert a.shape == (2, 3) and b.shape == (4,) and c.dtype == torch.int64
+    assert a.untyped_storage().data_ptr() == b.untyped_storage().data_ptr()
+    got["in"].wait()
+    got["in"].wait()
+    assert waits == [2, 3]                      # only the receive's own operations, once each
+    assert len(bus.inflight) == 1
+    bus.transfer([])                            # nothing completed yet: still retained
+    assert len(bus.inflight) == 1
+    for w in works:
+        w.complete = True
+    bus.transfer([])
+    assert bus.inflight == []
+    bus.flush()
+    assert waits == [2, 3]
+
+
+def test_transport_flush_waits_outstanding_sends_once(fake_dist):
+    posted, works, waits = fake_dist
+    bus = Transport("cpu")
+    spec = [((4,), torch.float32)]
+    bus.transfer([("out", 0, 1, spec, (torch.zeros(4),))])
+    bus.flush()
+    bus.flush()
+    assert waits == [0] and bus.inflight == []
+
+
+def test_transport_checks_sent_shapes(fake_dist):
+    bus = Transport("cpu")
+    with pytest.raises(ValueError, match="spec says"):
+        bus.transfer([("out", 0, 1, [((4,), torch.float32)], (torch.zeros(5),))])
 
 
 def test_max_and_sum_over_ranks_gloo(tmp_path):

@@ -137,3 +137,6 @@ def test_varlen_seqs_from_cu_seqlens():
         ops.varlen_seqs([0, 880, 440], [(22, 40)] * 2, [3, 4])      # decreasing
     with pytest.raises(PrepError):
         ops.varlen_seqs([0, 880], [(22, 40)], [3], ring_rows=[0])  # ring without frames
+    for grid in ((0, 40), (22, -1)):                               # an empty or negative grid
+        with pytest.raises(PrepError, match=f"member 1: grid {grid[0]}x{grid[1]}"):
+            ops.varlen_seqs([0, 880, 1760], [(22, 40), grid], [3, 4])
