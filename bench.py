@@ -1308,6 +1308,54 @@ def run_rope_window(args):
     return 0
 
 
+def run_attention(args):
+    """The ring attention kernel (ops.attention) on the 1.3B block call at steady state: 1560
+    query rows x 12 heads x 128 over a 22-frame window of 34 320 ring rows, against torch SDPA
+    on the same inputs read as ring views ([B, H, rows, D] transposed views, what the SDPA path of
+    RingAttention passes) and as contiguous [B, H, L, D] tensors (what the reference's
+    concatenated window gives SDPA).  FLOPs per call: 4 * Lq * Lk * D * H."""
+    import torch.nn.functional as F
+
+    from physisserve_b200.ops import attention
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    H, D, Lq, Lk = 12, 128, 1560, 22 * 1560
+    B = args.attn_batch
+    C = H * D
+    g = torch.Generator().manual_seed(13)
+    q = torch.randn(B, Lq, C, generator=g).bfloat16().to(device)
+    k = torch.randn(B, Lk + 1560, C, generator=g).bfloat16().to(device)
+    v = torch.randn(B, Lk + 1560, C, generator=g).bfloat16().to(device)
+    out = torch.empty(B, Lq, C, device=device, dtype=torch.bfloat16)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
+    qh = q.view(B, Lq, H, D).transpose(1, 2)
+    kv_views = (k[:, :Lk].view(B, Lk, H, D).transpose(1, 2), v[:, :Lk].view(B, Lk, H, D).transpose(1, 2))
+    kv_contig = tuple(t.contiguous() for t in kv_views)
+    qc = qh.contiguous()
+    flops = 4.0 * B * Lq * Lk * D * H
+    runs = {
+        "ours": lambda i: attention(q, k, v, Lk, heads=H, out=out, workspace=ws),
+        "sdpa_ring_views": lambda i: F.scaled_dot_product_attention(qh, *kv_views),
+        "sdpa_contiguous": lambda i: F.scaled_dot_product_attention(qc, *kv_contig),
+    }
+    times = {name: _event_loop(fn, args.steps, args.warmup) for name, fn in runs.items()}
+    with open(ROOT / "MEASURED_PEAKS.json") as fh:
+        peaks = json.load(fh)
+    peak = float(peaks["bf16_tflops"])
+    emit({"impl": "attention", "metric": "attention_tflops", "unit": "TFLOP/s",
+          "value": flops / (times["ours"] * 1e-6) / 1e12, "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+          "config": {"workload": f"wan2.1-1.3b block-call attention, {B} member(s) x 1560 queries x 12 heads over "
+                                 "a 34 320-row ring window, bf16, head_dim 128", "flops_per_call": flops},
+          "us_per_call": times,
+          "tflops": {name: flops / (t * 1e-6) / 1e12 for name, t in times.items()},
+          "roofline": {"bound": "tensor", "peak": peak, "unit": "TFLOP/s", "peak_source": "MEASURED_PEAKS.json "
+                       "bf16_tflops (cuBLAS burst)", "frac": flops / (times["ours"] * 1e-6) / 1e12 / peak},
+          "speedup_vs_sdpa": {name: t / times["ours"] for name, t in times.items()},
+          "gpu": torch.cuda.get_device_name(device)})
+    return 0
+
+
 def run_e2e(args, work, world, device, stream):
     """The public API end to end: every launch of a step copies its q, k, v from pinned host
     memory to the device, runs the fused prep through physisserve_b200.ops.qk_norm_rope_kv
@@ -1444,6 +1492,9 @@ def main(argv=None):
                         help="time ps_rope on the reference layout's 22-frame K window")
     parser.add_argument("--processor", action="store_true",
                         help="time one whole self-attention block call: torch ops vs drop-in vs ring layout")
+    parser.add_argument("--attention", action="store_true",
+                        help="time the ring attention kernel against torch SDPA on the 1.3B block-call window")
+    parser.add_argument("--attn-batch", type=int, default=1, help="members of the --attention call")
     parser.add_argument("--pipeline", action="store_true",
                         help="BASELINE config 5 pipelined: 2-stage pipelines (15 blocks per GPU) over NCCL")
     args = parser.parse_args(argv)
@@ -1457,6 +1508,8 @@ def main(argv=None):
         return run_ltx_processor(args) if args.ltx else run_processor(args)
     if args.rope_window:
         return run_rope_window(args)
+    if args.attention:
+        return run_attention(args)
     if args.ltx:
         return run_ltx(args)
     if args.impl == "torch":

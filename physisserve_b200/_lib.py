@@ -37,7 +37,8 @@ SEQ_PREP, SEQ_SINK = 0, 1
 
 EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
            "ps_device_timeouts", "ps_wait_selftest", "ps_rope", "ps_rope_validate",
-           "ps_table_prep_validate", "ps_qk_norm_rope_tables", "ps_rope_tables", "ps_rope_tables_validate")
+           "ps_table_prep_validate", "ps_qk_norm_rope_tables", "ps_rope_tables", "ps_rope_tables_validate",
+           "ps_attention_workspace", "ps_attention_validate", "ps_ring_attention", "ps_attention_timeouts")
 
 
 class PsSeq(ctypes.Structure):
@@ -136,6 +137,27 @@ class PsTablePrepArgs(ctypes.Structure):
     ]
 
 
+class PsAttnArgs(ctypes.Structure):
+    """``ps_attn_args`` (include/physis_b200_attention.h)."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("q_tokens", ctypes.c_int32),
+        ("kv_tokens", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("ctas", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("q_member_stride", ctypes.c_int64), ("q_row_stride", ctypes.c_int64),
+        ("k", ctypes.c_void_p), ("k_member_stride", ctypes.c_int64), ("k_row_stride", ctypes.c_int64),
+        ("v", ctypes.c_void_p), ("v_member_stride", ctypes.c_int64), ("v_row_stride", ctypes.c_int64),
+        ("out", ctypes.c_void_p), ("out_member_stride", ctypes.c_int64), ("out_row_stride", ctypes.c_int64),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
+    ]
+
+
 _LIB = None
 
 
@@ -176,6 +198,14 @@ def load() -> ctypes.CDLL:
     lib.ps_rope_tables.argtypes = [*table_rope_args, ctypes.c_void_p]
     lib.ps_rope_tables_validate.restype = ctypes.c_int32
     lib.ps_rope_tables_validate.argtypes = table_rope_args
+    for name in ("ps_attention_validate", "ps_ring_attention"):
+        getattr(lib, name).restype = ctypes.c_int32
+    lib.ps_attention_validate.argtypes = [ctypes.c_void_p]
+    lib.ps_ring_attention.argtypes = [ctypes.c_void_p, ctypes.c_void_p]  # (const ps_attn_args*, stream)
+    lib.ps_attention_workspace.restype = ctypes.c_int32
+    lib.ps_attention_workspace.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]
+    lib.ps_attention_timeouts.restype = ctypes.c_int32
+    lib.ps_attention_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
     version = lib.ps_abi_version()
     if version != ABI_VERSION:
         raise ImportError(f"{LIB_PATH} has ABI version {version}, expected {ABI_VERSION}")

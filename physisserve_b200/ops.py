@@ -601,6 +601,71 @@ def qk_norm_rope_tables(
         _check(_lib.load().ps_qk_norm_rope_tables(ctypes.byref(args), _stream(device)))
 
 
+# --------------------------------------------------------------------------------------
+# Attention over the ring (include/physis_b200_attention.h)
+# --------------------------------------------------------------------------------------
+def _member_rows(t: torch.Tensor, C: int, name: str):
+    """(member stride, row stride) in elements of a [B, rows, C] or [B, rows, H, D] tensor whose
+    rows are contiguous C-element vectors."""
+    if t.dim() == 4:
+        if t.shape[2] * t.shape[3] != C or t.stride(3) != 1 or t.stride(2) != t.shape[3]:
+            raise PrepError(f"{name}: [B, rows, H, D] with contiguous heads expected, got {tuple(t.shape)}")
+    elif t.dim() != 3 or t.shape[2] != C or t.stride(2) != 1:
+        raise PrepError(f"{name}: [B, rows, {C}] with unit stride on the last dimension expected, got "
+                        f"{tuple(t.shape)}")
+    return t.stride(0), t.stride(1)
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_tokens: int | None = None, *,
+              heads: int, out: torch.Tensor | None = None, scale: float | None = None, ctas: int = 0,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Softmax attention of the query rows over the window rows ``[0, kv_tokens)`` of K and V
+    (``ps_ring_attention``): ``F.scaled_dot_product_attention`` of models/wan.py:110 over the
+    ring rows instead of a concatenated window (engine/kv_cache.py:51-56).
+
+    ``q``: [B, Lq, C] (or [B, Lq, H, D]) bf16 token-major rows; ``k``/``v``: [B, rows, C] ring
+    storage (rows >= kv_tokens, default all rows); returns ``out`` [B, Lq, C] (allocated if
+    not given).  head_dim 128.  The scratch for units split between CTAs comes from
+    ``workspace`` (a byte tensor of at least ``attention_workspace`` bytes) or is allocated.
+    """
+    if q.dtype is not torch.bfloat16 or k.dtype is not torch.bfloat16 or v.dtype is not torch.bfloat16:
+        raise PrepError("attention takes bfloat16 q, k and v")
+    device = _require_cuda(q, k, v, out)
+    B, Lq = q.shape[0], q.shape[1]
+    C = q.shape[2] * (q.shape[3] if q.dim() == 4 else 1)
+    if C % heads:
+        raise PrepError(f"C={C} is not a multiple of heads={heads}")
+    rows = k.shape[1]
+    kv_tokens = rows if kv_tokens is None else int(kv_tokens)
+    if not 1 <= kv_tokens <= min(rows, v.shape[1]) or k.shape[0] != B or v.shape[0] != B:
+        raise PrepError(f"kv_tokens={kv_tokens} outside K/V of {tuple(k.shape)} / {tuple(v.shape)} for {B} members")
+    if out is None:
+        out = torch.empty(B, Lq, C, device=device, dtype=torch.bfloat16)
+    qs, ks, vs, os_ = (_member_rows(t, C, n) for t, n in ((q, "q"), (k, "k"), (v, "v"), (out, "out")))
+    args = _lib.PsAttnArgs(_lib.BF16, heads, C // heads, B, Lq, kv_tokens, float(scale or 0.0), int(ctas),
+                           q.data_ptr(), *qs, k.data_ptr(), *ks, v.data_ptr(), *vs, out.data_ptr(), *os_, None, 0)
+    lib = _lib.load()
+    with _on_device(device.index):
+        need = ctypes.c_int64(0)
+        _check(lib.ps_attention_workspace(ctypes.byref(args), ctypes.byref(need)))
+        if workspace is None or workspace.numel() * workspace.element_size() < need.value:
+            workspace = torch.empty(max(1, need.value), dtype=torch.uint8, device=device)
+        args.workspace = workspace.data_ptr()
+        args.workspace_bytes = workspace.numel() * workspace.element_size()
+        if Lq:
+            _check(lib.ps_ring_attention(ctypes.byref(args), _stream(device)))
+    return out
+
+
+def attention_timeouts(reset: bool = True, device: int | None = None) -> int:
+    """Bounded waits of the attention kernel that ran out on ``device`` (synchronises it)."""
+    index = torch.cuda.current_device() if device is None else int(device)
+    count = ctypes.c_uint32(0)
+    with _on_device(index):
+        _check(_lib.load().ps_attention_timeouts(ctypes.byref(count), int(reset)))
+    return int(count.value)
+
+
 def wait_selftest(limit_us: int = 20000, device: int | None = None) -> None:
     """Launch the bounded-wait self-test on ``device`` (default: current): one wait that
     nothing completes gives up after ``limit_us`` and adds one to ``device_timeouts``."""

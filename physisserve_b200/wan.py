@@ -27,7 +27,7 @@ from typing import Sequence
 import torch
 import torch.nn.functional as F
 
-from .ops import SEQ_SINK, PrepError, Seq, _default_split, flat_seq, qk_norm_rope_kv, ring_slot, rope
+from .ops import SEQ_SINK, PrepError, Seq, _default_split, attention, flat_seq, qk_norm_rope_kv, ring_slot, rope
 
 ATTENTION_SINK_CHUNKS = 1   # engine/kv_cache.py:28
 HISTORY_CHUNKS = 18         # engine/kv_cache.py:29
@@ -291,7 +291,9 @@ class RingAttention:
 
     ``cache`` is a ``RingCache`` (one per stream cell, set per block call like the
     reference's ``cache``) and ``rotary_emb`` is ``(freqs_cos, freqs_sin, RingPositions
-    per member)``.  SDPA reads the window straight from the ring storage.
+    per member)``.  The attention reads the window straight from the ring storage: the
+    sm_100a ring attention kernel (``ops.attention``) for bf16 with head_dim 128, torch SDPA
+    over the ring views otherwise.
     """
 
     def __init__(self):
@@ -309,6 +311,18 @@ class RingAttention:
         q_rot = prep_ring(q, k, v, _norm_weight(attn.norm_q, C, q.dtype, q.device),
                           _norm_weight(attn.norm_k, C, k.dtype, k.device), _norm_eps(attn.norm_q, q.dtype),
                           freqs_cos, freqs_sin, cache, positions)
+        if D == 128 and q.dtype == torch.bfloat16:
+            # The ring attention kernel reads each member's window rows where the prep wrote them.
+            windows = [cache.window_rows(pos.chunk) for pos in positions]
+            if len(set(windows)) == 1:
+                hidden = attention(q_rot, cache.k, cache.v, windows[0], heads=heads)
+            else:
+                hidden = torch.empty_like(q_rot)
+                for b, rows in enumerate(windows):
+                    attention(q_rot[b:b + 1], cache.k[b:b + 1], cache.v[b:b + 1], rows, heads=heads,
+                              out=hidden[b:b + 1])
+            return attn.to_out[1](attn.to_out[0](hidden))
+        # Other head sizes / dtypes: torch SDPA over the ring views (the reference's call).
         q_rot = q_rot.view(B, L, heads, D).transpose(1, 2)
         if len({cache.window_rows(pos.chunk) for pos in positions}) == 1:
             # Members whose windows have the same length: one SDPA over the ring views.

@@ -755,7 +755,10 @@ def test_prep_plan_matches_direct_calls(kernel):
     with pytest.raises(ops.PrepError):
         plan.launch(q=inputs[0][0].float())                    # other dtype
     with pytest.raises(ops.PrepError):
-        plan.launch(q_out=planned[0])                          # outputs are fixed in a plan
+        plan.launch(k_out=planned[1])                          # the ring outputs are fixed in a plan
+    plan.launch(q_out=direct[0])                               # q_out may be swapped
+    torch.cuda.synchronize()
+    assert torch.equal(planned[0], direct[0])
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
