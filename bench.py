@@ -1328,7 +1328,7 @@ def run_attention(args):
     k = torch.randn(B, Lk + 1560, C, generator=g).bfloat16().to(device)
     v = torch.randn(B, Lk + 1560, C, generator=g).bfloat16().to(device)
     out = torch.empty(B, Lq, C, device=device, dtype=torch.bfloat16)
-    ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
+    ws = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     qh = q.view(B, Lq, H, D).transpose(1, 2)
     kv_views = (k[:, :Lk].view(B, Lk, H, D).transpose(1, 2), v[:, :Lk].view(B, Lk, H, D).transpose(1, 2))
     kv_contig = tuple(t.contiguous() for t in kv_views)
@@ -1340,6 +1340,11 @@ def run_attention(args):
         "sdpa_contiguous": lambda i: F.scaled_dot_product_attention(qc, *kv_contig),
     }
     times = {name: _event_loop(fn, args.steps, args.warmup) for name, fn in runs.items()}
+    chunk_sweep = {}
+    for chunks in (1, 2, 3, 4, 5, 7, 9, 12, 16):
+        chunk_sweep[chunks] = _event_loop(
+            lambda i: attention(q, k, v, Lk, heads=H, out=out, workspace=ws, key_chunks=chunks), args.steps,
+            args.warmup)
     with open(ROOT / "MEASURED_PEAKS.json") as fh:
         peaks = json.load(fh)
     peak = float(peaks["bf16_tflops"])
@@ -1352,6 +1357,7 @@ def run_attention(args):
           "roofline": {"bound": "tensor", "peak": peak, "unit": "TFLOP/s", "peak_source": "MEASURED_PEAKS.json "
                        "bf16_tflops (cuBLAS burst)", "frac": flops / (times["ours"] * 1e-6) / 1e12 / peak},
           "speedup_vs_sdpa": {name: t / times["ours"] for name, t in times.items()},
+          "us_per_call_by_key_chunks": chunk_sweep,
           "gpu": torch.cuda.get_device_name(device)})
     return 0
 

@@ -40,6 +40,8 @@ typedef struct ps_attn_args {
   int32_t kv_tokens;  /* window rows per member (>= 1): rows [0, kv_tokens) of each ring */
   float scale;        /* softmax scale; <= 0 selects 1/sqrt(head_dim) */
   int32_t ctas;       /* persistent CTAs; 0 = one per SM */
+  int32_t key_chunks; /* key chunks per (member, head, query block), 1..16; 0 = automatic */
+  int32_t reserved;   /* 0 */
   const void* q;  int64_t q_member_stride;   int64_t q_row_stride;
   const void* k;  int64_t k_member_stride;   int64_t k_row_stride;
   const void* v;  int64_t v_member_stride;   int64_t v_row_stride;
@@ -59,12 +61,13 @@ PS_API int32_t ps_attention_validate(const ps_attn_args* args);
  * head, written to `out`.  Replaces the SDPA call over the concatenated window
  * (models/wan.py:110 with engine/kv_cache.py:51-56).
  *
- * Work: the (member, head, 128-row query tile) units times the window's
- * 128-row key tiles are cut into equal contiguous ranges, one per persistent
- * CTA; a unit whose keys span two CTAs leaves partial results (unnormalised
- * output rows, running max and sum) in `workspace`, combined by a second
- * launch on the same stream.  S = Q K^T and O += P V run on the tensor cores
- * (tcgen05.mma, accumulators in tensor memory), tiles arrive by TMA.
+ * Work: (member, head, 256-row query block) units, each over key_chunks equal
+ * chunks of the window's 128-row key tiles; the pieces are spread over
+ * persistent CTAs in rounds that walk the same keys of one head together.  With
+ * more than one chunk every piece leaves partial results (unnormalised output
+ * rows, running max and sum) in `workspace`, combined by a second launch on the
+ * same stream.  S = Q K^T and O += P V run on the tensor cores (tcgen05.mma,
+ * accumulators and P in tensor memory), tiles arrive by TMA.
  *
  * Numerics: S in fp32, probabilities rounded to bf16 for P V (as flash
  * attention kernels do), softmax sums and O in fp32, one rounding of O / sum

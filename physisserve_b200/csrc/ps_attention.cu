@@ -7,25 +7,30 @@
 // the reference processor (models/wan.py:110) without the window concatenation of its
 // cache (engine/kv_cache.py:51-56).
 //
-// Work units are (member, head, 128-row query tile); each unit runs over the window's
-// 128-row key tiles.  The (unit, key tile) pairs are cut into G equal contiguous ranges,
-// one per persistent CTA (G = SMs), so every SM gets the same number of tile pairs
-// whatever the unit count (156 units of the 1.3B block call would otherwise take two
-// waves on 148 SMs with the second nearly empty).  A unit whose key tiles span two or
-// more CTAs leaves partial results (unnormalised O rows, running max and sum) in the
-// workspace; combine_kernel merges them.
+// A unit is (member, head, 256-row query block) = two 128-row query tiles that share every
+// K/V tile the CTA loads.  The window's 128-row key tiles of a unit are cut into S equal
+// chunks; a piece is (key chunk, unit), pieces are numbered chunk-major and CTA g runs
+// pieces g, g + G, g + 2G, ...  so the CTAs of one round hold the same key chunk of
+// consecutive units -- the query blocks of a few heads -- and walk those keys in step: each
+// K/V tile comes from DRAM once and from L2 for the other query blocks of its head.  The host
+// picks S so that the pieces fill whole rounds of the SMs (156 query tiles of the 1.3B block
+// call do not divide over 148 SMs).  With S > 1 every piece leaves partial results
+// (unnormalised O rows, running max and sum) in the workspace; combine_kernel merges them.
 //
-// CTA of 6 warps, one CTA per SM:
-//   warp 0    TMA producer: Q tile once per unit segment, K and V tiles through 2-stage
-//             rings, all 128-byte swizzled ({64 columns, 128 rows} boxes);
-//   warp 1    owns the tensor memory (512 columns: O, two S buffers) and issues the MMAs:
-//             S_t = Q K_t^T into S[t%2], then O += P_{t-1} V_{t-1}, so the tensor core
-//             works on the next scores while the softmax warps exponentiate;
-//   warps 2-5 softmax, one query row per thread (TMEM lane = row): S row from TMEM, row
-//             max, exp2, row sum, P row (bf16) into a swizzled shared-memory tile that
-//             the next MMA reads as its A operand.  O is rescaled in TMEM only when a
-//             row's max grows by more than 2^8 (the probabilities are exact for any
-//             fixed reference; a stale one only has to keep them in range).
+// CTA of 10 warps, one CTA per SM:
+//   warp 0     TMA producer: the two Q tiles once per piece, K and V tiles through 2-stage
+//              rings, all 128-byte swizzled ({64 columns, 128 rows} boxes);
+//   warp 1     owns the tensor memory (512 columns: O0 | S0 | O1 | S1) and issues the MMAs
+//              in the order PV0(t), S0(t+1), PV1(t), S1(t+1): while one softmax warpgroup
+//              exponentiates, the tensor core works for the other;
+//   warps 2-5  softmax of query tile 0, warps 6-9 of tile 1: one query row per thread (TMEM
+//              lane = row).  A thread loads its S row, takes the row max, writes the bf16
+//              probabilities P back into the S columns it has read (P V then takes A from
+//              tensor memory), and adds up the row sum.  O is rescaled in tensor memory only
+//              when a row's max grows by more than 2^8 (the probabilities are exact for any
+//              fixed reference; a stale one only has to keep them in range).
+// tcgen05.mma operations of one thread complete in issue order, so a commit after S_i(t+1)
+// also reports P_i(t) V(t) done, and S_i(t+1) may overwrite the P_i(t) columns it follows.
 // All waits are bounded (~2 s of %globaltimer): a wait that runs out counts itself in
 // g_attn_timeouts, raises the CTA's abort flag, every role leaves its loop, the producer
 // drains its loads, the MMA warp waits for its MMAs and frees the tensor memory.
@@ -50,24 +55,28 @@ namespace {
 constexpr int kBM = 128;         // query rows per tile (MMA M, TMEM lanes)
 constexpr int kBN = 128;         // key rows per tile (MMA N of S, K of P V)
 constexpr int kD = 128;          // head dim (MMA K of S, N of P V)
+constexpr int kQTiles = 2;       // query tiles per unit (per CTA)
 constexpr int kTile = kBM * kD * 2;       // bytes of one 128 x 128 bf16 tile (two 16 KB halves)
 constexpr int kHalf = kTile / 2;          // one {64 columns, 128 rows} swizzled box
-constexpr int kKStages = 2, kVStages = 2, kPBufs = 2;
-constexpr int kThreads = 192;
+constexpr int kKStages = 2, kVStages = 2;
+constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
-constexpr int kColO = 0, kColS = 128;     // TMEM columns of O and of S buffer 0 (buffer 1 at 256)
 constexpr unsigned long long kAttnWaitNs = 2000000000ull;
+constexpr int kMaxChunks = 16;
 
-// Shared memory (from a 1024-byte aligned base): Q | K stages | V stages | P buffers | barriers.
+// TMEM columns of query tile i: O_i at 256*i, S_i / P_i at 256*i + 128.
+__host__ __device__ constexpr int col_o(int i) { return 256 * i; }
+__host__ __device__ constexpr int col_s(int i) { return 256 * i + 128; }
+
+// Shared memory (from a 1024-byte aligned base): Q tiles | K stages | V stages | barriers.
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;
+constexpr int kOffK = kOffQ + kQTiles * kTile;
 constexpr int kOffV = kOffK + kKStages * kTile;
-constexpr int kOffP = kOffV + kVStages * kTile;
-constexpr int kOffBar = kOffP + kPBufs * kTile;
+constexpr int kOffBar = kOffV + kVStages * kTile;
 enum Bar {
   kQFull, kQEmpty, kKFull0, kKEmpty0 = kKFull0 + kKStages, kVFull0 = kKEmpty0 + kKStages,
-  kVEmpty0 = kVFull0 + kVStages, kSFull0 = kVEmpty0 + kVStages, kSEmpty0 = kSFull0 + 2, kPFull0 = kSEmpty0 + 2,
-  kPEmpty0 = kPFull0 + kPBufs, kMmaDone = kPEmpty0 + kPBufs, kNumBars
+  kVEmpty0 = kVFull0 + kVStages, kSFull0 = kVEmpty0 + kVStages, kPFull0 = kSFull0 + kQTiles,
+  kOFinal0 = kPFull0 + kQTiles, kMmaDone = kOFinal0 + kQTiles, kNumBars
 };
 constexpr int kOffTmem = kOffBar + 8 * kNumBars;
 constexpr int kOffAbort = kOffTmem + 4;
@@ -75,13 +84,15 @@ constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + slack to align the base t
 static_assert(kSmemBytes <= 227 * 1024, "attention tiles exceed shared memory");
 
 struct AParams {
-  int32_t H, Lq, Lk, qtiles, nkv, G;
-  int64_t W;             // (unit, key tile) pairs
+  int32_t H, Lq, Lk, qblocks, nkv, G;
+  int32_t chunks;        // key chunks per unit (S)
+  int64_t units;         // (member, head, 256-row query block) units
+  int64_t pieces;        // units * chunks
   float scale_log2;      // softmax scale * log2(e)
   void* out;
   int64_t out_member_stride, out_row_stride;
-  float* ws_o;           // [2G][128][128] unnormalised O of partial segments
-  float2* ws_ml;         // [2G][128] (running max in log2 units, sum)
+  float* ws_o;           // [pieces][2][128][128] unnormalised O of the pieces (chunks > 1)
+  float2* ws_ml;         // [pieces][2][128] (running max in log2 units, sum)
 };
 
 // ---------------------------------------------------------------------------------------
@@ -160,6 +171,16 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x 16 bf16) packed two per 32-bit column.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc ? 1u : 0u)
+      : "memory");
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -208,41 +229,27 @@ __host__ __device__ constexpr uint32_t mma_idesc(uint32_t b_mn) {
 // ---------------------------------------------------------------------------------------
 // The attention kernel
 // ---------------------------------------------------------------------------------------
-struct Segment {
-  int b, h, qt;
-  int j0, j1;       // key tiles [j0, j1) of the unit
-  bool complete;    // the segment covers every key tile of its unit
-  int slot;         // workspace slot of a partial segment
+struct Piece {
+  int b, h, qb;
+  int j0, j1;       // key tiles [j0, j1)
+  bool two;         // query tile 1 holds rows below Lq
+  int64_t index;    // piece number (workspace slot)
 };
 
-// The segments of CTA `cta`: its contiguous range of (unit, key tile) pairs, unit by unit.
-struct SegmentWalker {
-  const AParams& p;
-  int64_t pos, end, first_unit;
-  int cta;
-  __device__ SegmentWalker(const AParams& params, int c) : p(params), cta(c) {
-    pos = static_cast<int64_t>(c) * p.W / p.G;
-    end = static_cast<int64_t>(c + 1) * p.W / p.G;
-    first_unit = pos / p.nkv;
-  }
-  __device__ bool next(Segment& s) {
-    if (pos >= end) return false;
-    const int64_t u = pos / p.nkv;
-    s.j0 = static_cast<int>(pos - u * p.nkv);
-    const int64_t stop = end - u * p.nkv;
-    s.j1 = stop < p.nkv ? static_cast<int>(stop) : p.nkv;
-    s.complete = s.j0 == 0 && s.j1 == p.nkv;
-    s.slot = 2 * cta + (u == first_unit ? 0 : 1);
-    const int64_t bh = u / p.qtiles;
-    s.qt = static_cast<int>(u - bh * p.qtiles);
-    s.b = static_cast<int>(bh / p.H);
-    s.h = static_cast<int>(bh - static_cast<int64_t>(s.b) * p.H);
-    pos = u * p.nkv + s.j1;
-    return true;
-  }
-};
+__device__ __forceinline__ void piece_of(const AParams& p, int64_t index, Piece& pc) {
+  const int64_t c = index / p.units;
+  const int64_t u = index - c * p.units;
+  const int64_t bh = u / p.qblocks;
+  pc.qb = static_cast<int>(u - bh * p.qblocks);
+  pc.b = static_cast<int>(bh / p.H);
+  pc.h = static_cast<int>(bh - static_cast<int64_t>(pc.b) * p.H);
+  pc.j0 = static_cast<int>(c * p.nkv / p.chunks);
+  pc.j1 = static_cast<int>((c + 1) * p.nkv / p.chunks);
+  pc.two = (pc.qb * 2 + 1) * kBM < p.Lq;
+  pc.index = index;
+}
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(200)
     attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ AParams p) {
   extern __shared__ unsigned char smem_raw[];
@@ -266,11 +273,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bar_init(bar(kVFull0 + s), 1);
       bar_init(bar(kVEmpty0 + s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      bar_init(bar(kSFull0 + s), 1);
-      bar_init(bar(kSEmpty0 + s), 4);       // one arrive per softmax warp
-      bar_init(bar(kPFull0 + s), 128);      // every softmax thread
-      bar_init(bar(kPEmpty0 + s), 1);
+    for (int i = 0; i < kQTiles; ++i) {
+      bar_init(bar(kSFull0 + i), 1);
+      bar_init(bar(kPFull0 + i), 128);      // every softmax thread of the tile
+      bar_init(bar(kOFinal0 + i), 1);
     }
     bar_init(bar(kMmaDone), 1);
     *abort_flag = 0;
@@ -296,40 +302,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool leader = lane == 0;
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------
-    SegmentWalker walk(p, blockIdx.x);
-    Segment sg;
-    int t = 0, seg = 0, q_issued = 0;
+    int t = 0, n_pieces = 0;
     int last_k[kKStages], last_v[kVStages];
     for (int s = 0; s < kKStages; ++s) last_k[s] = -1;
     for (int s = 0; s < kVStages; ++s) last_v[s] = -1;
     bool ok = true;
-    while (ok && walk.next(sg)) {
-      if (seg > 0 && !(ok = warp_wait(kQEmpty, (seg - 1) & 1))) break;
-      const int col = sg.h * kD;
+    Piece pc;
+    for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
+      piece_of(p, index, pc);
+      if (n_pieces > 0 && !(ok = warp_wait(kQEmpty, (n_pieces - 1) & 1))) break;
+      const int col = pc.h * kD;
       if (leader) {
-        bar_expect_tx(bar(kQFull), kTile);
-        tma_load(sbase + kOffQ, &tq, col, sg.qt * kBM, sg.b, bar(kQFull));
-        tma_load(sbase + kOffQ + kHalf, &tq, col + 64, sg.qt * kBM, sg.b, bar(kQFull));
+        bar_expect_tx(bar(kQFull), pc.two ? 2 * kTile : kTile);
+        for (int i = 0; i < (pc.two ? 2 : 1); ++i) {
+          const int row = (2 * pc.qb + i) * kBM;
+          tma_load(sbase + kOffQ + i * kTile, &tq, col, row, pc.b, bar(kQFull));
+          tma_load(sbase + kOffQ + i * kTile + kHalf, &tq, col + 64, row, pc.b, bar(kQFull));
+        }
       }
-      ++q_issued;
-      for (int j = sg.j0; j < sg.j1; ++j, ++t) {
+      ++n_pieces;
+      for (int j = pc.j0; j < pc.j1; ++j, ++t) {
         const int sk = t % kKStages, sv = t % kVStages;
         if (t >= kKStages && !(ok = warp_wait(kKEmpty0 + sk, ((t / kKStages) & 1) ^ 1))) break;
         if (leader) {
           bar_expect_tx(bar(kKFull0 + sk), kTile);
-          tma_load(sbase + kOffK + sk * kTile, &tk, col, j * kBN, sg.b, bar(kKFull0 + sk));
-          tma_load(sbase + kOffK + sk * kTile + kHalf, &tk, col + 64, j * kBN, sg.b, bar(kKFull0 + sk));
+          tma_load(sbase + kOffK + sk * kTile, &tk, col, j * kBN, pc.b, bar(kKFull0 + sk));
+          tma_load(sbase + kOffK + sk * kTile + kHalf, &tk, col + 64, j * kBN, pc.b, bar(kKFull0 + sk));
         }
         last_k[sk] = t;
         if (t >= kVStages && !(ok = warp_wait(kVEmpty0 + sv, ((t / kVStages) & 1) ^ 1))) break;
         if (leader) {
           bar_expect_tx(bar(kVFull0 + sv), kTile);
-          tma_load(sbase + kOffV + sv * kTile, &tv, col, j * kBN, sg.b, bar(kVFull0 + sv));
-          tma_load(sbase + kOffV + sv * kTile + kHalf, &tv, col + 64, j * kBN, sg.b, bar(kVFull0 + sv));
+          tma_load(sbase + kOffV + sv * kTile, &tv, col, j * kBN, pc.b, bar(kVFull0 + sv));
+          tma_load(sbase + kOffV + sv * kTile + kHalf, &tv, col + 64, j * kBN, pc.b, bar(kVFull0 + sv));
         }
         last_v[sv] = t;
       }
-      ++seg;
     }
     // Every load issued must have landed before the CTA may exit (bounded as well).
     if (leader) {
@@ -338,166 +346,191 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last_k[s] >= 0) bar_wait(bar(kKFull0 + s), (last_k[s] / kKStages) & 1, &never);
       for (int s = 0; s < kVStages; ++s)
         if (last_v[s] >= 0) bar_wait(bar(kVFull0 + s), (last_v[s] / kVStages) & 1, &never);
-      if (q_issued > 0) bar_wait(bar(kQFull), (q_issued - 1) & 1, &never);
+      if (n_pieces > 0) bar_wait(bar(kQFull), (n_pieces - 1) & 1, &never);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
     const uint32_t id_s = mma_idesc(0), id_pv = mma_idesc(1);
-    SegmentWalker walk(p, blockIdx.x);
-    Segment sg;
-    int t = 0, seg = 0;
+    int t = 0, t1 = 0, n_pieces = 0;  // key tiles (all / with query tile 1), pieces
     bool ok = true;
-    // O += P_tt V_tt (first: overwrite O).
-    auto pv = [&](int tt, bool first) -> bool {
-      const int sv = tt % kVStages, pb = tt & 1;
-      if (!warp_wait(kPFull0 + pb, (tt >> 1) & 1)) return false;
-      if (!warp_wait(kVFull0 + sv, (tt / kVStages) & 1)) return false;
+    Piece pc;
+    // S_i = Q_i K^T of key tile tt (K stage tt % kKStages) into the S_i columns.
+    auto issue_s = [&](int i, int tt) {
+      const uint32_t qa = sbase + kOffQ + i * kTile, ka = sbase + kOffK + (tt % kKStages) * kTile;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+        tc_mma(tmem + col_s(i), smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), id_s, kk > 0);
+      }
+    };
+    // O_i (+)= P_i V of key tile tt: A = P_i from tensor memory (bf16 pairs packed in the S_i
+    // columns, 8 columns per 16 keys), B = V (MN-major: the head dim along the swizzled rows,
+    // its two 64-column halves 16 KB apart, 8-row key groups 1 KB apart).
+    auto issue_pv = [&](int i, int tt, bool first) {
+      const uint32_t va = sbase + kOffV + (tt % kVStages) * kTile;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, smem_desc(va + kk * 16 * 128, kHalf, 1024), id_pv,
+                  !(first && kk == 0));
+    };
+    for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
+      piece_of(p, index, pc);
+      const int nq = pc.two ? 2 : 1;
+      if (!(ok = warp_wait(kQFull, n_pieces & 1))) break;
+      ++n_pieces;
+      // Prologue: S of the piece's first key tile for both query tiles.
+      if (!(ok = warp_wait(kKFull0 + t % kKStages, (t / kKStages) & 1))) break;
       tc_fence_after();
       if (leader) {
-        const uint32_t pa = sbase + kOffP + pb * kTile, va = sbase + kOffV + sv * kTile;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // A = P (K-major: keys along the swizzled rows); B = V (MN-major: the head dim along
-          // the rows, its two 64-column halves 16 KB apart, 8-row key groups 1 KB apart).
-          const uint64_t a = smem_desc(pa + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = smem_desc(va + kk * 16 * 128, kHalf, 1024);
-          tc_mma(tmem + kColO, a, b, id_pv, !(first && kk == 0));
+        for (int i = 0; i < nq; ++i) {
+          issue_s(i, t);
+          tc_commit(bar(kSFull0 + i));
         }
-        tc_commit(bar(kVEmpty0 + sv));
-        tc_commit(bar(kPEmpty0 + pb));   // also tells the softmax warps that O holds P_tt V_tt
+        tc_commit(bar(kKEmpty0 + t % kKStages));
       }
       __syncwarp();
-      return true;
-    };
-    while (ok && walk.next(sg)) {
-      if (!(ok = warp_wait(kQFull, seg & 1))) break;
-      for (int j = sg.j0; j < sg.j1; ++j, ++t) {
-        const int sk = t % kKStages, sb = t & 1;
-        if (!(ok = warp_wait(kKFull0 + sk, (t / kKStages) & 1))) break;
-        if (t >= 2 && !(ok = warp_wait(kSEmpty0 + sb, ((t >> 1) & 1) ^ 1))) break;
+      const int n = pc.j1 - pc.j0;
+      for (int jj = 0; jj < n; ++jj, ++t) {
+        const bool more = jj + 1 < n;
+        // P_0 V for this key tile, then S_0 of the next one.
+        if (!(ok = warp_wait(kPFull0, t & 1))) break;  // query tile 0 takes part in every key tile
+        if (!(ok = warp_wait(kVFull0 + t % kVStages, (t / kVStages) & 1))) break;
         tc_fence_after();
         if (leader) {
-          const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + sk * kTile;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            tc_mma(tmem + kColS + sb * 128, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), id_s, kk > 0);
-          }
-          tc_commit(bar(kKEmpty0 + sk));
-          tc_commit(bar(kSFull0 + sb));
-          if (j == sg.j1 - 1) tc_commit(bar(kQEmpty));
+          issue_pv(0, t, jj == 0);
+          if (!more) tc_commit(bar(kOFinal0));
         }
         __syncwarp();
-        if (j > sg.j0 && !(ok = pv(t - 1, j - 1 == sg.j0))) break;
+        if (more && !(ok = warp_wait(kKFull0 + (t + 1) % kKStages, ((t + 1) / kKStages) & 1))) break;
+        tc_fence_after();
+        if (leader) {
+          if (more) {
+            issue_s(0, t + 1);
+            tc_commit(bar(kSFull0));
+          }
+          if (nq == 1) {
+            tc_commit(bar(kVEmpty0 + t % kVStages));
+            if (more) tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
+            else tc_commit(bar(kQEmpty));
+          }
+        }
+        __syncwarp();
+        if (nq == 2) {
+          if (!(ok = warp_wait(kPFull0 + 1, t1 & 1))) break;
+          ++t1;
+          tc_fence_after();
+          if (leader) {
+            issue_pv(1, t, jj == 0);
+            tc_commit(bar(kVEmpty0 + t % kVStages));
+            if (!more) {
+              tc_commit(bar(kOFinal0 + 1));
+              tc_commit(bar(kQEmpty));
+            } else {
+              issue_s(1, t + 1);
+              tc_commit(bar(kSFull0 + 1));
+              tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
+            }
+          }
+          __syncwarp();
+        }
       }
-      if (!ok) break;
-      if (!(ok = pv(t - 1, sg.j1 - 1 == sg.j0))) break;
-      ++seg;
     }
     if (leader) tc_commit(bar(kMmaDone));
     __syncwarp();
   } else {
     // ------------------------------- softmax warps -------------------------------
+    const int qi = (warp - 2) >> 2;             // query tile of this warpgroup
     const int quarter = warp & 3;               // the TMEM lanes this warp may access
     const int row = quarter * 32 + lane;        // query row of the tile = TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    SegmentWalker walk(p, blockIdx.x);
-    Segment sg;
-    int t = 0;
+    const uint32_t s_addr = lane_addr + col_s(qi), o_addr = lane_addr + col_o(qi);
+    int n_tiles = 0, n_pieces = 0;              // key tiles / pieces this warpgroup has processed
     bool ok = true;
-    while (ok && walk.next(sg)) {
+    Piece pc;
+    for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
+      piece_of(p, index, pc);
+      if (qi == 1 && !pc.two) continue;         // query tile 1 past Lq: nothing to do
       float m = -INFINITY, l = 0.f;
-      for (int j = sg.j0; j < sg.j1; ++j, ++t) {
-        const int sb = t & 1;
-        if (!(ok = warp_wait(kSFull0 + sb, (t >> 1) & 1))) break;
+      for (int j = pc.j0; j < pc.j1; ++j, ++n_tiles) {
+        if (!(ok = warp_wait(kSFull0 + qi, n_tiles & 1))) break;
         tc_fence_after();
         uint32_t s[128];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + kColS + sb * 128 + 32 * c, s + 32 * c);
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, s + 32 * c);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (leader) bar_arrive(bar(kSEmpty0 + sb));
         const int valid = p.Lk - j * kBN;  // keys of this tile inside the window
         if (valid < kBN) {
 #pragma unroll
           for (int i = 0; i < 128; ++i)
             if (i >= valid) s[i] = __float_as_uint(-INFINITY);
         }
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        float mx[8];
 #pragma unroll
-        for (int i = 0; i < 128; i += 4) {
-          mx0 = fmaxf(mx0, __uint_as_float(s[i]));
-          mx1 = fmaxf(mx1, __uint_as_float(s[i + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(s[i + 2]));
-          mx3 = fmaxf(mx3, __uint_as_float(s[i + 3]));
-        }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
-        const float m_new = fmaxf(m, mx);
+        for (int e = 0; e < 8; ++e) mx[e] = __uint_as_float(s[e]);
+#pragma unroll
+        for (int i = 8; i < 128; i += 8)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], __uint_as_float(s[i + e]));
+        const float row_max =
+            fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+            p.scale_log2;
+        const float m_new = fmaxf(m, row_max);
         const bool grow = m_new > m + 8.f;
-        if (__any_sync(0xffffffffu, grow)) {
-          const float alpha = grow ? fast_exp2(m - m_new) : 1.f;
-          if (grow) {
-            l *= alpha;
-            m = m_new;
-          }
-          if (j > sg.j0) {
-            // O holds this segment's earlier tiles: rescale it once P_{t-1} V_{t-1} has landed
-            // (P buffer (t-1)%2 released; its previous phase, P_{t-3} V_{t-3}, was waited for
-            // before P_{t-1} was written).
-            if (!(ok = warp_wait(kPEmpty0 + ((t - 1) & 1), ((t - 1) >> 1) & 1))) break;
-            tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t o[32];
-              tmem_ld32(lane_addr + kColO + 32 * c, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(lane_addr + kColO + 32 * c, o);
-            }
-            tmem_wait_st();
-          }
+        const float alpha = grow ? fast_exp2(m - m_new) : 1.f;
+        if (grow) {
+          l *= alpha;
+          m = m_new;
         }
-        // Probabilities, their sum, and the bf16 P row in the 128-byte swizzled K-major layout.
-        if (t >= 2 && !(ok = warp_wait(kPEmpty0 + sb, ((t >> 1) & 1) ^ 1))) break;
-        unsigned char* prow = smem + kOffP + sb * kTile + (row >> 3) * 1024 + (row & 7) * 128;
-        float l0 = 0.f, l1 = 0.f;
+        // Probabilities (bf16 pairs, even key in the low half) over the S columns already read.
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint32_t w[4];
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float x0 = fast_exp2(fmaf(__uint_as_float(s[8 * c + 2 * e]), p.scale_log2, -m));
-            const float x1 = fast_exp2(fmaf(__uint_as_float(s[8 * c + 2 * e + 1]), p.scale_log2, -m));
-            l0 += x0;
-            l1 += x1;
+          for (int c = 0; c < 32; ++c) {
+            const float x0 = fast_exp2(fmaf(__uint_as_float(s[64 * h + 2 * c]), p.scale_log2, -m));
+            const float x1 = fast_exp2(fmaf(__uint_as_float(s[64 * h + 2 * c + 1]), p.scale_log2, -m));
+            ls[(c & 1) * 2] += x0;
+            ls[(c & 1) * 2 + 1] += x1;
             __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-            w[e] = *reinterpret_cast<uint32_t*>(&h2);
+            pk[c] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          const int half = c >> 3, chunk = (c & 7) ^ (row & 7);
-          *reinterpret_cast<uint4*>(prow + half * kHalf + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+          tmem_st32(s_addr + 32 * h, pk);
         }
-        l += l0 + l1;
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        // O holds this piece's earlier tiles: bring it to the new reference.  P_i V of the
+        // previous tile has completed (the commit of S_i for this tile follows it).
+        if (__any_sync(0xffffffffu, grow) && j > pc.j0) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + 32 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_addr + 32 * c, o);
+          }
+        }
+        tmem_wait_st();
         tc_fence_before();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        bar_arrive(bar(kPFull0 + sb));
+        bar_arrive(bar(kPFull0 + qi));
       }
       if (!ok) break;
-      // Epilogue of the segment: O once its last tile's P V has landed.
-      if (!(ok = warp_wait(kPEmpty0 + ((t - 1) & 1), ((t - 1) >> 1) & 1))) break;
+      // Epilogue of the piece: O once the piece's last P V has landed.
+      if (!(ok = warp_wait(kOFinal0 + qi, n_pieces & 1))) break;
+      ++n_pieces;
       tc_fence_after();
-      const int q_row = sg.qt * kBM + row;
+      const int q_row = (2 * pc.qb + qi) * kBM + row;
       const bool live = q_row < p.Lq;
-      if (sg.complete) {
+      if (p.chunks == 1) {
         const float inv = 1.f / l;
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + sg.b * p.out_member_stride +
-                             static_cast<int64_t>(q_row) * p.out_row_stride + sg.h * kD;
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + pc.b * p.out_member_stride +
+                             static_cast<int64_t>(q_row) * p.out_row_stride + pc.h * kD;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(lane_addr + kColO + 32 * c, o);
+          tmem_ld32(o_addr + 32 * c, o);
           tmem_wait_ld();
           if (live) {
 #pragma unroll
@@ -514,17 +547,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        float* dst = p.ws_o + (static_cast<int64_t>(sg.slot) * kBM + row) * kD;
+        const int64_t slot = pc.index * kQTiles + qi;
+        float* dst = p.ws_o + (slot * kBM + row) * kD;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(lane_addr + kColO + 32 * c, o);
+          tmem_ld32(o_addr + 32 * c, o);
           tmem_wait_ld();
 #pragma unroll
           for (int v = 0; v < 8; ++v)
             *reinterpret_cast<uint4*>(dst + 32 * c + 4 * v) = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
         }
-        p.ws_ml[static_cast<int64_t>(sg.slot) * kBM + row] = make_float2(m, l);
+        p.ws_ml[slot * kBM + row] = make_float2(m, l);
       }
       tc_fence_before();
     }
@@ -543,37 +577,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merges the partial segments of the units whose key tiles were split between CTAs:
-// out = sum_i 2^(m_i - m) O_i / sum_i 2^(m_i - m) l_i with m = max_i m_i.  One CTA per unit;
-// a unit that one CTA finished is skipped.
+// Merges the key chunks of every (unit, query tile): out = sum_c 2^(m_c - m) O_c /
+// sum_c 2^(m_c - m) l_c with m = max_c m_c.  One CTA per (unit, query tile), a row per
+// thread pair.
 __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ AParams p) {
-  const int64_t u = blockIdx.x;
-  const int64_t first = u * p.nkv, last = first + p.nkv - 1;
-  auto cta_of = [&](int64_t pos) {
-    int64_t c = pos * p.G / p.W;
-    while (c + 1 < p.G && (c + 1) * p.W / p.G <= pos) ++c;
-    while (c > 0 && c * p.W / p.G > pos) --c;
-    return c;
-  };
-  const int64_t c_lo = cta_of(first), c_hi = cta_of(last);
-  if (c_lo == c_hi) return;
+  const int64_t u = blockIdx.x >> 1;
+  const int qi = blockIdx.x & 1;
   const int row = threadIdx.x >> 1, half = threadIdx.x & 1;
-  const int64_t bh = u / p.qtiles;
-  const int qt = static_cast<int>(u - bh * p.qtiles);
+  const int64_t bh = u / p.qblocks;
+  const int qb = static_cast<int>(u - bh * p.qblocks);
   const int b = static_cast<int>(bh / p.H), h = static_cast<int>(bh - static_cast<int64_t>(b) * p.H);
-  const int q_row = qt * kBM + row;
+  const int q_row = (2 * qb + qi) * kBM + row;
   if (q_row >= p.Lq) return;
   float m = -INFINITY;
-  for (int64_t c = c_lo; c <= c_hi; ++c) {
-    const int64_t slot = 2 * c + ((c * p.W / p.G) / p.nkv == u ? 0 : 1);
-    m = fmaxf(m, p.ws_ml[slot * kBM + row].x);
-  }
+  for (int c = 0; c < p.chunks; ++c) m = fmaxf(m, p.ws_ml[((c * p.units + u) * kQTiles + qi) * kBM + row].x);
   float acc[64];
 #pragma unroll
   for (int i = 0; i < 64; ++i) acc[i] = 0.f;
   float l = 0.f;
-  for (int64_t c = c_lo; c <= c_hi; ++c) {
-    const int64_t slot = 2 * c + ((c * p.W / p.G) / p.nkv == u ? 0 : 1);
+  for (int c = 0; c < p.chunks; ++c) {
+    const int64_t slot = (c * p.units + u) * kQTiles + qi;
     const float2 ml = p.ws_ml[slot * kBM + row];
     const float w = exp2f(ml.x - m);
     l += w * ml.y;
@@ -607,7 +630,6 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ AP
 // ---------------------------------------------------------------------------------------
 struct APlan {
   AParams params;
-  int64_t units;
   int64_t ws_bytes;
 };
 
@@ -631,6 +653,31 @@ static int check_rows(const void* ptr, int64_t member_stride, int64_t row_stride
   return PS_OK;
 }
 
+// Key chunks per unit: the S (1..16) with the least modelled time, in key-tile times of one
+// CTA: whole rounds of pieces (a piece = its key tiles + ~2 tiles of set-up and epilogue), and
+// with S > 1 the partial results: ~3 tile times for a CTA to write a piece's 128 KB, and the
+// combine pass reading them all (~8 MB per tile time over the whole GPU).
+static int choose_chunks(int64_t units, int nkv, int max_ctas) {
+  int best = 1;
+  double best_cost = 0;
+  for (int c = 1; c <= kMaxChunks && c <= nkv; ++c) {
+    const int64_t pieces = units * c;
+    const int64_t G = pieces < max_ctas ? pieces : max_ctas;
+    const int64_t rounds = (pieces + G - 1) / G;
+    double cost = static_cast<double>(rounds) * ((nkv + c - 1) / c + 2);
+    if (c > 1) cost += 3.0 * rounds + static_cast<double>(pieces) * kQTiles * kBM * kD * 4 / 8.0e6;
+    if (c == 1 || cost < best_cost) {
+      best = c;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+static int64_t workspace_bytes(int64_t pieces, int chunks) {
+  return chunks > 1 ? pieces * kQTiles * kBM * (kD * 4 + 8) : 0;
+}
+
 static int build_attn(const ps_attn_args* a, APlan* plan, bool host_only) {
   clear_error();
   if (!a) return fail(PS_ERR_NULL, "args is NULL");
@@ -639,7 +686,8 @@ static int build_attn(const ps_attn_args* a, APlan* plan, bool host_only) {
   if (a->heads < 1 || a->batch < 1 || a->q_tokens < 0 || a->kv_tokens < 1)
     return fail(PS_ERR_SHAPE, "heads=%d batch=%d q_tokens=%d kv_tokens=%d", a->heads, a->batch, a->q_tokens,
                 a->kv_tokens);
-  if (a->ctas < 0) return fail(PS_ERR_SHAPE, "ctas=%d", a->ctas);
+  if (a->ctas < 0 || a->key_chunks < 0 || a->key_chunks > kMaxChunks)
+    return fail(PS_ERR_SHAPE, "ctas=%d key_chunks=%d (0..%d)", a->ctas, a->key_chunks, kMaxChunks);
   const int64_t C = static_cast<int64_t>(a->heads) * kD;
   int rc;
   if ((rc = check_rows(a->q, a->q_member_stride, a->q_row_stride, C, a->batch, a->q_tokens, "q")) ||
@@ -652,28 +700,30 @@ static int build_attn(const ps_attn_args* a, APlan* plan, bool host_only) {
   p.H = a->heads;
   p.Lq = a->q_tokens;
   p.Lk = a->kv_tokens;
-  p.qtiles = (a->q_tokens + kBM - 1) / kBM;
+  p.qblocks = (a->q_tokens + kQTiles * kBM - 1) / (kQTiles * kBM);
   p.nkv = (a->kv_tokens + kBN - 1) / kBN;
-  plan->units = static_cast<int64_t>(a->batch) * a->heads * p.qtiles;
-  p.W = plan->units * p.nkv;
-  int G = a->ctas > 0 ? a->ctas : (host_only ? 148 : sm_count_attn());
-  if (p.W < G) G = static_cast<int>(p.W > 0 ? p.W : 1);
-  p.G = G;
+  p.units = static_cast<int64_t>(a->batch) * a->heads * p.qblocks;
+  const int max_ctas = a->ctas > 0 ? a->ctas : (host_only ? 148 : sm_count_attn());
+  int chunks = a->key_chunks > 0 ? a->key_chunks : choose_chunks(p.units, p.nkv, max_ctas);
+  if (chunks > p.nkv) chunks = p.nkv;
+  p.chunks = chunks;
+  p.pieces = p.units * chunks;
+  p.G = static_cast<int32_t>(p.pieces < max_ctas ? (p.pieces > 0 ? p.pieces : 1) : max_ctas);
   const double scale = a->scale > 0.f ? a->scale : 1.0 / sqrt(static_cast<double>(kD));
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.out = a->out;
   p.out_member_stride = a->out_member_stride;
   p.out_row_stride = a->out_row_stride;
-  plan->ws_bytes = static_cast<int64_t>(2 * G) * kBM * (kD * 4 + 8);
+  plan->ws_bytes = workspace_bytes(p.pieces, chunks);
   if (!host_only || a->workspace) {
-    if (plan->units > 0 && (!a->workspace || a->workspace_bytes < plan->ws_bytes))
+    if (plan->ws_bytes > 0 && (!a->workspace || a->workspace_bytes < plan->ws_bytes))
       return fail(PS_ERR_NULL, "workspace of %lld bytes needed (ps_attention_workspace), %lld given",
                   (long long)plan->ws_bytes, (long long)a->workspace_bytes);
     if (a->workspace && !aligned16(a->workspace)) return fail(PS_ERR_ALIGN, "workspace is not 16-byte aligned");
   }
   p.ws_o = static_cast<float*>(a->workspace);
   p.ws_ml = reinterpret_cast<float2*>(static_cast<unsigned char*>(a->workspace) +
-                                      static_cast<int64_t>(2 * G) * kBM * kD * 4);
+                                      p.pieces * kQTiles * kBM * kD * 4);
   return PS_OK;
 }
 
@@ -726,15 +776,15 @@ static cudaError_t allow_attn_smem() {
 
 extern "C" int32_t ps_attention_workspace(const ps_attn_args* args, int64_t* bytes) {
   if (!bytes) return ps::fail(PS_ERR_NULL, "bytes is NULL");
+  if (!args) return ps::fail(PS_ERR_NULL, "args is NULL");
   ps::APlan plan;
   ps_attn_args a = *args;
   a.workspace = nullptr;
   a.workspace_bytes = 0;
+  if (a.ctas == 0) a.ctas = ps::sm_count_attn();
   const int rc = ps::build_attn(&a, &plan, true);
   if (rc != PS_OK) return rc;
-  int G = args->ctas > 0 ? args->ctas : ps::sm_count_attn();
-  if (plan.params.W < G) G = static_cast<int>(plan.params.W > 0 ? plan.params.W : 1);
-  *bytes = static_cast<int64_t>(2 * G) * ps::kBM * (ps::kD * 4 + 8);
+  *bytes = plan.ws_bytes;
   return PS_OK;
 }
 
@@ -747,7 +797,7 @@ extern "C" int32_t ps_ring_attention(const ps_attn_args* args, void* stream) {
   ps::APlan plan;
   int rc = ps::build_attn(args, &plan, false);
   if (rc != PS_OK) return rc;
-  if (plan.units == 0) return PS_OK;
+  if (plan.params.units == 0) return PS_OK;
   const int64_t C = static_cast<int64_t>(args->heads) * ps::kD;
   CUtensorMap tq, tk, tv;
   if ((rc = ps::make_map(&tq, args->q, C, args->q_tokens, args->batch, args->q_row_stride, args->q_member_stride, "q")) ||
@@ -760,12 +810,8 @@ extern "C" int32_t ps_ring_attention(const ps_attn_args* args, void* stream) {
   ps::attention_kernel<<<plan.params.G, ps::kThreads, ps::kSmemBytes, s>>>(tq, tk, tv, plan.params);
   err = cudaGetLastError();
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(err));
-  // The combine launch is needed when a CTA boundary falls inside a unit's key tiles.
-  bool split = false;
-  for (int c = 1; c < plan.params.G && !split; ++c)
-    split = (static_cast<int64_t>(c) * plan.params.W / plan.params.G) % plan.params.nkv != 0;
-  if (split) {
-    ps::combine_kernel<<<static_cast<unsigned>(plan.units), 256, 0, s>>>(plan.params);
+  if (plan.params.chunks > 1) {
+    ps::combine_kernel<<<static_cast<unsigned>(plan.params.units * ps::kQTiles), 256, 0, s>>>(plan.params);
     err = cudaGetLastError();
     if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "attention combine launch: %s", cudaGetErrorString(err));
   }

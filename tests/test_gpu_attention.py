@@ -57,20 +57,23 @@ def _inputs(B, Lq, rows, heads, seed, scale=1.0):
     return q, k, v
 
 
-@pytest.mark.parametrize("B,Lq,rows,kv,heads,ctas", [
-    (1, 128, 128, 128, 1, 0),        # one tile pair
-    (2, 200, 400, 300, 3, 0),        # partial query and key tiles; rows past the window ignored
-    (2, 200, 400, 300, 3, 1),        # one CTA walks every unit (complete segments only)
-    (2, 200, 400, 300, 3, 7),        # units split between CTAs: partial results combined
-    (1, 18, 132, 132, 2, 0),         # the recorded request's shapes (grid 2x3, 22-frame window)
-    (1, 6, 30, 30, 2, 5),            # fewer keys than a tile, more CTAs than tile pairs
-    (3, 300, 1000, 777, 2, 13),      # three members, odd split
+@pytest.mark.parametrize("B,Lq,rows,kv,heads,ctas,chunks", [
+    (1, 128, 128, 128, 1, 0, 0),     # one key tile, query tile 1 empty
+    (1, 256, 256, 256, 1, 0, 1),     # both query tiles full, two key tiles
+    (2, 200, 400, 300, 3, 0, 0),     # partial query and key tiles; rows past the window ignored
+    (2, 200, 400, 300, 3, 1, 1),     # one CTA walks every unit in turn
+    (2, 200, 400, 300, 3, 7, 3),     # key chunks: partial results combined
+    (2, 300, 1200, 1100, 2, 5, 9),   # more chunks than CTAs, query tile 1 partly filled
+    (1, 18, 132, 132, 2, 0, 0),      # the recorded request's shapes (grid 2x3, 22-frame window)
+    (1, 6, 30, 30, 2, 5, 0),         # fewer keys than a tile
+    (3, 600, 1000, 777, 2, 13, 0),   # three members, two query blocks each
+    (1, 1560, 4000, 3999, 2, 0, 16), # the most chunks
 ])
-def test_attention_matches_fp32_reference(B, Lq, rows, kv, heads, ctas):
+def test_attention_matches_fp32_reference(B, Lq, rows, kv, heads, ctas, chunks):
     q, k, v = _inputs(B, Lq, rows, heads, seed=B * 1000 + Lq + kv)
     k[:, kv:] = float("nan")         # rows past the window must never be read
     v[:, kv:] = float("nan")
-    got = ops.attention(q, k, v, kv, heads=heads, ctas=ctas)
+    got = ops.attention(q, k, v, kv, heads=heads, ctas=ctas, key_chunks=chunks)
     torch.cuda.synchronize()
     assert got.shape == q.shape and got.dtype == torch.bfloat16
     _check(got, q, k, v, heads, kv, f"B={B} Lq={Lq} kv={kv} H={heads} ctas={ctas}")
@@ -85,8 +88,9 @@ def test_attention_large_scores_rescale():
     ramp = torch.linspace(0.2, 6.0, kv, device=DEV)[None, :, None]
     k = (k.float() * ramp).bfloat16()
     q = (q.float() * 3.0).bfloat16()
-    got = ops.attention(q, k, v, kv, heads=heads, ctas=3)
-    _check(got, q, k, v, heads, kv, "growing scores")
+    for chunks in (1, 3):
+        got = ops.attention(q, k, v, kv, heads=heads, ctas=3, key_chunks=chunks)
+        _check(got, q, k, v, heads, kv, f"growing scores, {chunks} chunk(s)")
 
 
 def test_attention_wan_block_call_window():
