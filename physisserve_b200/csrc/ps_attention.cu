@@ -204,6 +204,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -249,7 +257,7 @@ __device__ __forceinline__ void piece_of(const AParams& p, int64_t index, Piece&
   pc.index = index;
 }
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ AParams p) {
   extern __shared__ unsigned char smem_raw[];
@@ -485,18 +493,18 @@ __global__ void __maxnreg__(200)
         // Probabilities (bf16 pairs, even key in the low half) over the S columns already read.
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t pk[32];
+        for (int h = 0; h < 4; ++h) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float x0 = fast_exp2(fmaf(__uint_as_float(s[64 * h + 2 * c]), p.scale_log2, -m));
-            const float x1 = fast_exp2(fmaf(__uint_as_float(s[64 * h + 2 * c + 1]), p.scale_log2, -m));
+          for (int c = 0; c < 16; ++c) {
+            const float x0 = fast_exp2(fmaf(__uint_as_float(s[32 * h + 2 * c]), p.scale_log2, -m));
+            const float x1 = fast_exp2(fmaf(__uint_as_float(s[32 * h + 2 * c + 1]), p.scale_log2, -m));
             ls[(c & 1) * 2] += x0;
             ls[(c & 1) * 2 + 1] += x1;
             __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
             pk[c] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          tmem_st32(s_addr + 32 * h, pk);
+          tmem_st16(s_addr + 16 * h, pk);
         }
         l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         // O holds this piece's earlier tiles: bring it to the new reference.  P_i V of the
