@@ -145,6 +145,28 @@ __device__ __noinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile in
   }
 }
 
+// Deadline of a polling loop: step(progressed) returns false once nothing progressed for
+// kAttnWaitNs (raising the abort flag, counted once by `count`) or the CTA aborted.
+struct Poll {
+  unsigned long long since = 0;
+  __device__ bool step(bool progressed, volatile int* abort_flag, bool count) {
+    if (progressed) {
+      since = 0;
+      return true;
+    }
+    if (*abort_flag) return false;
+    const unsigned long long now = now_ns();
+    if (since == 0) {
+      since = now;
+    } else if (now - since > kAttnWaitNs) {
+      if (count) atomicAdd(&g_attn_timeouts, 1u);
+      *abort_flag = 1;
+      return false;
+    }
+    return true;
+  }
+};
+
 __device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
@@ -221,6 +243,27 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for x <= ~9 without the MUFU (range reduction plus a polynomial, the textbook method):
+// x = n + f with n = round(x) read from the low mantissa bits of x + 1.5*2^23 and f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted here to 2^f on that
+// interval by iteratively reweighted least squares (relative error <= 7.5e-5, 26 times below
+// half a bf16 ulp); 2^n added to the exponent field.  x < -125 gives 0.
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float t = __fadd_rn(xc, 12582912.f);
+  const float f = __fsub_rn(xc, __fsub_rn(t, 12582912.f));
+  const float q = fmaf(fmaf(fmaf(0.055171236395835876f, f, 0.24261020123958588f), f, 0.6932609677314758f), f,
+                       0.9999281167984009f);
+  const float r = __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+  return x < -125.f ? 0.f : r;
+}
+
+__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // Shared-memory matrix descriptor of a 128-byte swizzled tile (sm_100 format: start address,
 // leading / stride byte offsets in 16-byte units, version 1, swizzle mode 2 = 128B).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -257,6 +300,7 @@ __device__ __forceinline__ void piece_of(const AParams& p, int64_t index, Piece&
   pc.index = index;
 }
 
+template <int EMU>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ AParams p) {
@@ -329,23 +373,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       ++n_pieces;
-      for (int j = pc.j0; j < pc.j1; ++j, ++t) {
-        const int sk = t % kKStages, sv = t % kVStages;
-        if (t >= kKStages && !(ok = warp_wait(kKEmpty0 + sk, ((t / kKStages) & 1) ^ 1))) break;
-        if (leader) {
-          bar_expect_tx(bar(kKFull0 + sk), kTile);
-          tma_load(sbase + kOffK + sk * kTile, &tk, col, j * kBN, pc.b, bar(kKFull0 + sk));
-          tma_load(sbase + kOffK + sk * kTile + kHalf, &tk, col + 64, j * kBN, pc.b, bar(kKFull0 + sk));
+      // K and V tiles are issued independently as their stages free up (K runs ahead while the
+      // P V products of both query tiles still hold a V stage).
+      int kt = t, vt = t;
+      const int end_t = t + (pc.j1 - pc.j0);
+      Poll poll;
+      while (kt < end_t || vt < end_t) {
+        bool progressed = false;
+        if (kt < end_t) {
+          const int sk = kt % kKStages;
+          if (kt < kKStages || __all_sync(0xffffffffu, bar_try(bar(kKEmpty0 + sk), ((kt / kKStages) & 1) ^ 1))) {
+            const int j = pc.j0 + (kt - t);
+            if (leader) {
+              bar_expect_tx(bar(kKFull0 + sk), kTile);
+              tma_load(sbase + kOffK + sk * kTile, &tk, col, j * kBN, pc.b, bar(kKFull0 + sk));
+              tma_load(sbase + kOffK + sk * kTile + kHalf, &tk, col + 64, j * kBN, pc.b, bar(kKFull0 + sk));
+            }
+            last_k[sk] = kt++;
+            progressed = true;
+          }
         }
-        last_k[sk] = t;
-        if (t >= kVStages && !(ok = warp_wait(kVEmpty0 + sv, ((t / kVStages) & 1) ^ 1))) break;
-        if (leader) {
-          bar_expect_tx(bar(kVFull0 + sv), kTile);
-          tma_load(sbase + kOffV + sv * kTile, &tv, col, j * kBN, pc.b, bar(kVFull0 + sv));
-          tma_load(sbase + kOffV + sv * kTile + kHalf, &tv, col + 64, j * kBN, pc.b, bar(kVFull0 + sv));
+        if (vt < end_t) {
+          const int sv = vt % kVStages;
+          if (vt < kVStages || __all_sync(0xffffffffu, bar_try(bar(kVEmpty0 + sv), ((vt / kVStages) & 1) ^ 1))) {
+            const int j = pc.j0 + (vt - t);
+            if (leader) {
+              bar_expect_tx(bar(kVFull0 + sv), kTile);
+              tma_load(sbase + kOffV + sv * kTile, &tv, col, j * kBN, pc.b, bar(kVFull0 + sv));
+              tma_load(sbase + kOffV + sv * kTile + kHalf, &tv, col + 64, j * kBN, pc.b, bar(kVFull0 + sv));
+            }
+            last_v[sv] = vt++;
+            progressed = true;
+          }
         }
-        last_v[sv] = t;
+        if (!(ok = poll.step(progressed, abort_flag, leader))) break;
       }
+      t = end_t;
     }
     // Every load issued must have landed before the CTA may exit (bounded as well).
     if (leader) {
@@ -360,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
     const uint32_t id_s = mma_idesc(0), id_pv = mma_idesc(1);
-    int t = 0, t1 = 0, n_pieces = 0;  // key tiles (all / with query tile 1), pieces
+    int t = 0, t0_count = 0, t1 = 0, n_pieces = 0;  // key tiles; P tiles of query tile 0 / 1; pieces
     bool ok = true;
     Piece pc;
     // S_i = Q_i K^T of key tile tt (K stage tt % kKStages) into the S_i columns.
@@ -398,51 +461,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(bar(kKEmpty0 + t % kKStages));
       }
       __syncwarp();
-      const int n = pc.j1 - pc.j0;
-      for (int jj = 0; jj < n; ++jj, ++t) {
-        const bool more = jj + 1 < n;
-        // P_0 V for this key tile, then S_0 of the next one.
-        if (!(ok = warp_wait(kPFull0, t & 1))) break;  // query tile 0 takes part in every key tile
-        if (!(ok = warp_wait(kVFull0 + t % kVStages, (t / kVStages) & 1))) break;
-        tc_fence_after();
-        if (leader) {
-          issue_pv(0, t, jj == 0);
-          if (!more) tc_commit(bar(kOFinal0));
-        }
-        __syncwarp();
-        if (more && !(ok = warp_wait(kKFull0 + (t + 1) % kKStages, ((t + 1) / kKStages) & 1))) break;
-        tc_fence_after();
-        if (leader) {
-          if (more) {
-            issue_s(0, t + 1);
-            tc_commit(bar(kSFull0));
-          }
-          if (nq == 1) {
-            tc_commit(bar(kVEmpty0 + t % kVStages));
-            if (more) tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
-            else tc_commit(bar(kQEmpty));
-          }
-        }
-        __syncwarp();
-        if (nq == 2) {
-          if (!(ok = warp_wait(kPFull0 + 1, t1 & 1))) break;
-          ++t1;
+      // Each query tile advances on its own: step i issues P_i V of its next key tile and, unless
+      // that was the piece's last, S_i of the tile after -- whichever tile's probabilities are
+      // ready first goes first.  A V stage is released once both tiles' P V read it, a K stage
+      // once both tiles' S read it.
+      const int end_t = t + (pc.j1 - pc.j0);
+      int ti[kQTiles] = {t, nq == 2 ? t : end_t};  // next key tile whose P V is due, per query tile
+      int v_rel = t, k_rel = t + 1;                 // next V / K tile to release (K of t released above)
+      Poll poll;
+      while (ti[0] < end_t || ti[1] < end_t) {
+        bool progressed = false;
+#pragma unroll
+        for (int i = 0; i < kQTiles; ++i) {
+          const int tt = ti[i];
+          if (tt >= end_t) continue;
+          const int cnt = i == 0 ? t0_count : t1;
+          const bool more = tt + 1 < end_t;
+          bool ready = bar_try(bar(kPFull0 + i), cnt & 1) && bar_try(bar(kVFull0 + tt % kVStages), (tt / kVStages) & 1);
+          if (ready && more) ready = bar_try(bar(kKFull0 + (tt + 1) % kKStages), ((tt + 1) / kKStages) & 1);
+          if (!__all_sync(0xffffffffu, ready)) continue;
           tc_fence_after();
           if (leader) {
-            issue_pv(1, t, jj == 0);
-            tc_commit(bar(kVEmpty0 + t % kVStages));
-            if (!more) {
-              tc_commit(bar(kOFinal0 + 1));
-              tc_commit(bar(kQEmpty));
+            issue_pv(i, tt, tt == t);
+            if (more) {
+              issue_s(i, tt + 1);
+              tc_commit(bar(kSFull0 + i));
             } else {
-              issue_s(1, t + 1);
-              tc_commit(bar(kSFull0 + 1));
-              tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
+              tc_commit(bar(kOFinal0 + i));
             }
           }
+          ti[i] = tt + 1;
+          if (i == 0) ++t0_count; else ++t1;
+          const int low = ti[0] < ti[1] ? ti[0] : ti[1];
+          if (leader) {
+            for (int x = v_rel; x < low; ++x) tc_commit(bar(kVEmpty0 + x % kVStages));
+            for (int x = k_rel; x <= low && x < end_t; ++x) tc_commit(bar(kKEmpty0 + x % kKStages));
+          }
+          v_rel = low > v_rel ? low : v_rel;
+          const int k_to = low < end_t - 1 ? low : end_t - 1;
+          k_rel = k_to + 1 > k_rel ? k_to + 1 : k_rel;
+          progressed = true;
           __syncwarp();
         }
+        if (!(ok = poll.step(progressed, abort_flag, leader))) break;
       }
+      if (!ok) break;
+      if (leader) tc_commit(bar(kQEmpty));
+      __syncwarp();
+      t = end_t;
     }
     if (leader) tc_commit(bar(kMmaDone));
     __syncwarp();
@@ -463,23 +529,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = pc.j0; j < pc.j1; ++j, ++n_tiles) {
         if (!(ok = warp_wait(kSFull0 + qi, n_tiles & 1))) break;
         tc_fence_after();
-        uint32_t s[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, s + 32 * c);
-        tmem_wait_ld();
+        // Pass 1: the row max, 64 columns per TMEM load round.
         const int valid = p.Lk - j * kBN;  // keys of this tile inside the window
-        if (valid < kBN) {
-#pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i >= valid) s[i] = __float_as_uint(-INFINITY);
-        }
         float mx[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) mx[e] = __uint_as_float(s[e]);
+        for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
 #pragma unroll
-        for (int i = 8; i < 128; i += 8)
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s[64];
+          tmem_ld32(s_addr + 64 * hh, s);
+          tmem_ld32(s_addr + 64 * hh + 32, s + 32);
+          tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], __uint_as_float(s[i + e]));
+          for (int i = 0; i < 64; i += 8)
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (64 * hh + i + e < valid) mx[e] = fmaxf(mx[e], __uint_as_float(s[i + e]));
+        }
         const float row_max =
             fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
             p.scale_log2;
@@ -490,23 +556,46 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= alpha;
           m = m_new;
         }
-        // Probabilities (bf16 pairs, even key in the low half) over the S columns already read.
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+        // Pass 2: probabilities (bf16 pairs, even key in the low half), 32 S columns reloaded per
+        // round and written back as 16 P columns over S columns already consumed: x = s * scale *
+        // log2(e) - m in packed fp32 pairs; 2^x on the MUFU, or for EMU of every 8 pairs by the
+        // polynomial (exp2_poly), which runs on the FMA pipe beside it.
+        const f32x2 sc2 = f2_make(p.scale_log2, p.scale_log2), nm2 = f2_make(-m, -m);
+        f32x2 ls0 = 0, ls1 = 0;
+#pragma unroll 1
         for (int h = 0; h < 4; ++h) {
+          uint32_t s[32];
+          tmem_ld32(s_addr + 32 * h, s);
+          tmem_wait_ld();
+          if (valid < kBN) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * h + i >= valid) s[i] = __float_as_uint(-INFINITY);
+          }
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const float x0 = fast_exp2(fmaf(__uint_as_float(s[32 * h + 2 * c]), p.scale_log2, -m));
-            const float x1 = fast_exp2(fmaf(__uint_as_float(s[32 * h + 2 * c + 1]), p.scale_log2, -m));
-            ls[(c & 1) * 2] += x0;
-            ls[(c & 1) * 2 + 1] += x1;
+            float x0, x1;
+            f2_split(f2_fma(f2_make(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), sc2, nm2), x0, x1);
+            if ((c & 7) < EMU) {
+              x0 = exp2_poly(x0);
+              x1 = exp2_poly(x1);
+            } else {
+              x0 = fast_exp2(x0);
+              x1 = fast_exp2(x1);
+            }
+            if (c & 1) ls1 = f2_add(ls1, f2_make(x0, x1)); else ls0 = f2_add(ls0, f2_make(x0, x1));
             __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
             pk[c] = *reinterpret_cast<uint32_t*>(&h2);
           }
           tmem_st16(s_addr + 16 * h, pk);
         }
-        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        {
+          float a, b, c, d;
+          f2_split(ls0, a, b);
+          f2_split(ls1, c, d);
+          l += (a + b) + (c + d);
+        }
         // O holds this piece's earlier tiles: bring it to the new reference.  P_i V of the
         // previous tile has completed (the commit of S_i for this tile follows it).
         if (__any_sync(0xffffffffu, grow) && j > pc.j0) {
@@ -636,9 +725,22 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ AP
 // ---------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------
+// The compiled shares of exp2 taken by the polynomial (out of every 8 probability pairs).
+constexpr int kEmuChoices[] = {0, 2, 3};
+using AttnFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AParams);
+static AttnFn attn_fn(int emu) {
+  switch (emu) {
+    case 0: return attention_kernel<0>;
+    case 2: return attention_kernel<2>;
+    case 3: return attention_kernel<3>;
+    default: return nullptr;
+  }
+}
+
 struct APlan {
   AParams params;
   int64_t ws_bytes;
+  int emu;  // probability pairs of every 8 whose exp2 the polynomial takes
 };
 
 static int sm_count_attn() {
@@ -723,6 +825,9 @@ static int build_attn(const ps_attn_args* a, APlan* plan, bool host_only) {
   p.out_member_stride = a->out_member_stride;
   p.out_row_stride = a->out_row_stride;
   plan->ws_bytes = workspace_bytes(p.pieces, chunks);
+  plan->emu = a->exp2_poly_share == 0 ? 2 : (a->exp2_poly_share < 0 ? 0 : a->exp2_poly_share);
+  if (!attn_fn(plan->emu)) return fail(PS_ERR_UNSUPPORTED, "exp2_poly_share=%d (0 = automatic, -1 = none, 2, 3)",
+                                       a->exp2_poly_share);
   if (!host_only || a->workspace) {
     if (plan->ws_bytes > 0 && (!a->workspace || a->workspace_bytes < plan->ws_bytes))
       return fail(PS_ERR_NULL, "workspace of %lld bytes needed (ps_attention_workspace), %lld given",
@@ -766,16 +871,18 @@ static int make_map(CUtensorMap* map, const void* base, int64_t C, int64_t rows,
   return PS_OK;
 }
 
-static cudaError_t allow_attn_smem() {
-  static int done_dev[64];
+static cudaError_t allow_attn_smem(AttnFn fn) {
+  static int done[64][4];
   static std::mutex lock;
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
+  int k = 0;
+  while (k < 3 && attn_fn(kEmuChoices[k]) != fn) ++k;
   std::lock_guard<std::mutex> guard(lock);
-  if (dev >= 0 && dev < 64 && done_dev[dev]) return cudaSuccess;
-  err = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (err == cudaSuccess && dev >= 0 && dev < 64) done_dev[dev] = 1;
+  if (dev >= 0 && dev < 64 && k < 3 && done[dev][k]) return cudaSuccess;
+  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (err == cudaSuccess && dev >= 0 && dev < 64 && k < 3) done[dev][k] = 1;
   return err;
 }
 
@@ -812,10 +919,11 @@ extern "C" int32_t ps_ring_attention(const ps_attn_args* args, void* stream) {
       (rc = ps::make_map(&tk, args->k, C, args->kv_tokens, args->batch, args->k_row_stride, args->k_member_stride, "k")) ||
       (rc = ps::make_map(&tv, args->v, C, args->kv_tokens, args->batch, args->v_row_stride, args->v_member_stride, "v")))
     return rc;
-  cudaError_t err = ps::allow_attn_smem();
+  const ps::AttnFn fn = ps::attn_fn(plan.emu);
+  cudaError_t err = ps::allow_attn_smem(fn);
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "attention smem opt-in: %s", cudaGetErrorString(err));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ps::attention_kernel<<<plan.params.G, ps::kThreads, ps::kSmemBytes, s>>>(tq, tk, tv, plan.params);
+  fn<<<plan.params.G, ps::kThreads, ps::kSmemBytes, s>>>(tq, tk, tv, plan.params);
   err = cudaGetLastError();
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(err));
   if (plan.params.chunks > 1) {
