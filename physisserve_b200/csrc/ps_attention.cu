@@ -153,14 +153,18 @@ __device__ __noinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile in
 }
 
 // Deadline of a polling loop: step(progressed) returns false once nothing progressed for
-// kAttnWaitNs (raising the abort flag, counted once by `count`) or the CTA aborted.
+// kAttnWaitNs (raising the abort flag, counted once by `count`) or the CTA aborted.  The
+// clock is read once per 64 idle rounds (a %globaltimer read is slow next to a try_wait).
 struct Poll {
   unsigned long long since = 0;
+  unsigned idle = 0;
   __device__ bool step(bool progressed, volatile int* abort_flag, bool count) {
     if (progressed) {
+      idle = 0;
       since = 0;
       return true;
     }
+    if ((++idle & 63) != 0) return true;
     if (*abort_flag) return false;
     const unsigned long long now = now_ns();
     if (since == 0) {
