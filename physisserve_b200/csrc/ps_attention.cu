@@ -127,6 +127,19 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of phase `parity` (test_wait never suspends the thread, unlike try_wait,
+// which may park it for a while when the phase is incomplete: polling loops must not park).
+__device__ __forceinline__ bool bar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -354,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto warp_wait = [&](int i, int parity) {
     return __all_sync(0xffffffffu, bar_wait(bar(i), parity, abort_flag, lane == 0));
   };
-  auto warp_try = [&](int i, int parity) { return __all_sync(0xffffffffu, bar_try(bar(i), parity)); };
+  auto warp_try = [&](int i, int parity) { return __all_sync(0xffffffffu, bar_test(bar(i), parity)); };
   const bool leader = lane == 0;
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------
