@@ -995,14 +995,17 @@ def run_processor(args):
     ring.cache.k.normal_()
     ring.cache.v.normal_()
     ring.cache.sink_k.normal_()
+    ring_kernel = RingAttention(attention_kernel=True)
+    ring_kernel.cache = ring.cache
 
-    def ring_processor():
-        ring.cache.sink_at = [pos.sink_position - 1]  # the sink moved by one frame since the last chunk
-        return ring(attn, hidden, rotary_emb=(cos, sin, [pos]))
+    def ring_processor(processor=ring):
+        processor.cache.sink_at = [pos.sink_position - 1]  # the sink moved by one frame since the last chunk
+        return processor(attn, hidden, rotary_emb=(cos, sin, [pos]))
 
     results = {}
     with torch.inference_mode():
-        for name, fn in (("torch", torch_processor), ("reference", reference_processor), ("ring", ring_processor)):
+        for name, fn in (("torch", torch_processor), ("reference", reference_processor), ("ring", ring_processor),
+                         ("ring_attention_kernel", lambda: ring_processor(ring_kernel))):
             for _ in range(args.warmup):
                 fn()
             torch.cuda.synchronize()
@@ -1340,9 +1343,6 @@ def run_attention(args):
         "sdpa_contiguous": lambda i: F.scaled_dot_product_attention(qc, *kv_contig),
     }
     times = {name: _event_loop(fn, args.steps, args.warmup) for name, fn in runs.items()}
-    exp2_sweep = {share: _event_loop(
-        lambda i: attention(q, k, v, Lk, heads=H, out=out, workspace=ws, exp2_poly_share=share), args.steps,
-        args.warmup) for share in (-1, 2, 3)}
     chunk_sweep = {}
     for chunks in (1, 2, 3, 4, 5, 7, 9, 12, 16):
         chunk_sweep[chunks] = _event_loop(
@@ -1361,7 +1361,6 @@ def run_attention(args):
                        "bf16_tflops (cuBLAS burst)", "frac": flops / (times["ours"] * 1e-6) / 1e12 / peak},
           "speedup_vs_sdpa": {name: t / times["ours"] for name, t in times.items()},
           "us_per_call_by_key_chunks": chunk_sweep,
-          "us_per_call_by_exp2_poly_share": exp2_sweep,
           "gpu": torch.cuda.get_device_name(device)})
     return 0
 

@@ -41,8 +41,7 @@ typedef struct ps_attn_args {
   float scale;        /* softmax scale; <= 0 selects 1/sqrt(head_dim) */
   int32_t ctas;       /* persistent CTAs; 0 = one per SM */
   int32_t key_chunks; /* key chunks per (member, head, query block), 1..16; 0 = automatic */
-  int32_t exp2_poly_share; /* probability pairs of every 8 whose 2^x a polynomial on the FMA pipe
-                              computes instead of the MUFU: 2 or 3; -1 = none; 0 = automatic */
+  int32_t reserved;   /* 0 */
   const void* q;  int64_t q_member_stride;   int64_t q_row_stride;
   const void* k;  int64_t k_member_stride;   int64_t k_row_stride;
   const void* v;  int64_t v_member_stride;   int64_t v_row_stride;

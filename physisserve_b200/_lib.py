@@ -150,7 +150,7 @@ class PsAttnArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("ctas", ctypes.c_int32),
         ("key_chunks", ctypes.c_int32),
-        ("exp2_poly_share", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
         ("q", ctypes.c_void_p), ("q_member_stride", ctypes.c_int64), ("q_row_stride", ctypes.c_int64),
         ("k", ctypes.c_void_p), ("k_member_stride", ctypes.c_int64), ("k_row_stride", ctypes.c_int64),
         ("v", ctypes.c_void_p), ("v_member_stride", ctypes.c_int64), ("v_row_stride", ctypes.c_int64),

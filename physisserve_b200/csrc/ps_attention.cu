@@ -8,33 +8,32 @@
 // cache (engine/kv_cache.py:51-56).
 //
 // A unit is (member, head, 256-row query block) = two 128-row query tiles that share every
-// K/V tile the CTA loads.  The window's 64-row key tiles of a unit are cut into S equal
+// K/V tile the CTA loads.  The window's 128-row key tiles of a unit are cut into S equal
 // chunks; a piece is (key chunk, unit), pieces are numbered chunk-major and CTA g runs
 // pieces g, g + G, g + 2G, ...  so the CTAs of one round hold the same key chunk of
 // consecutive units -- the query blocks of a few heads -- and walk those keys in step: each
 // K/V tile comes from DRAM once and from L2 for the other query blocks of its head.  The host
-// picks S so that the pieces fill whole rounds of the SMs (the 156 query tiles of the 1.3B
-// block call do not divide over 148 SMs).  With S > 1 every piece leaves partial results
+// picks S so that the pieces fill whole rounds of the SMs (156 query tiles of the 1.3B block
+// call do not divide over 148 SMs).  With S > 1 every piece leaves partial results
 // (unnormalised O rows, running max and sum) in the workspace; combine_kernel merges them.
 //
 // CTA of 10 warps, one CTA per SM:
-//   warp 0     TMA producer: the two Q tiles once per piece, K and V tiles through 4-stage
-//              rings filled independently, all 128-byte swizzled ({64 columns, rows} boxes);
-//   warp 1     owns the tensor memory (512 columns: O0 | O1 | S0 x 2 | S1 x 2) and issues the
-//              MMAs: per query tile, S = Q K^T up to two key tiles ahead into alternating S
-//              buffers, and O += P V as soon as the softmax has written P, whichever tile is
-//              ready first;
+//   warp 0     TMA producer: the two Q tiles once per piece, K and V tiles through 2-stage
+//              rings, all 128-byte swizzled ({64 columns, 128 rows} boxes);
+//   warp 1     owns the tensor memory (512 columns: O0 | S0 | O1 | S1) and issues the MMAs
+//              in the order PV0(t), S0(t+1), PV1(t), S1(t+1): while one softmax warpgroup
+//              exponentiates, the tensor core works for the other;
 //   warps 2-5  softmax of query tile 0, warps 6-9 of tile 1: one query row per thread (TMEM
 //              lane = row).  A thread loads its S row, takes the row max, writes the bf16
-//              probabilities P back into the S columns it has read (P V takes A from tensor
-//              memory), and adds up the row sum.  O is rescaled in tensor memory only when a
-//              row's max grows by more than 2^8 (the probabilities are exact for any fixed
-//              reference; a stale one only has to keep them in range).
-// tcgen05.mma operations of one thread complete in issue order, so S may overwrite a buffer
-// whose P an earlier-issued P V reads.  All waits are bounded (~2 s of %globaltimer): a wait
-// that runs out counts itself in g_attn_timeouts, raises the CTA's abort flag, every role
-// leaves its loop, the producer drains its loads, the MMA warp waits for its MMAs and frees
-// the tensor memory.
+//              probabilities P back into the S columns it has read (P V then takes A from
+//              tensor memory), and adds up the row sum.  O is rescaled in tensor memory only
+//              when a row's max grows by more than 2^8 (the probabilities are exact for any
+//              fixed reference; a stale one only has to keep them in range).
+// tcgen05.mma operations of one thread complete in issue order, so a commit after S_i(t+1)
+// also reports P_i(t) V(t) done, and S_i(t+1) may overwrite the P_i(t) columns it follows.
+// All waits are bounded (~2 s of %globaltimer): a wait that runs out counts itself in
+// g_attn_timeouts, raises the CTA's abort flag, every role leaves its loop, the producer
+// drains its loads, the MMA warp waits for its MMAs and frees the tensor memory.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -54,36 +53,30 @@ __device__ unsigned int g_attn_timeouts;
 namespace {
 
 constexpr int kBM = 128;         // query rows per tile (MMA M, TMEM lanes)
-constexpr int kBN = 64;          // key rows per key tile (MMA N of S, K of P V)
+constexpr int kBN = 128;         // key rows per tile (MMA N of S, K of P V)
 constexpr int kD = 128;          // head dim (MMA K of S, N of P V)
 constexpr int kQTiles = 2;       // query tiles per unit (per CTA)
-constexpr int kQTile = kBM * kD * 2;      // bytes of a 128-row Q tile (two 16 KB column halves)
-constexpr int kQHalf = kQTile / 2;        // one {64 columns, 128 rows} swizzled box
-constexpr int kKVTile = kBN * kD * 2;     // bytes of a 64-row K or V tile (two 8 KB column halves)
-constexpr int kKVHalf = kKVTile / 2;      // one {64 columns, 64 rows} swizzled box
-constexpr int kKStages = 4, kVStages = 4;
+constexpr int kTile = kBM * kD * 2;       // bytes of one 128 x 128 bf16 tile (two 16 KB halves)
+constexpr int kHalf = kTile / 2;          // one {64 columns, 128 rows} swizzled box
+constexpr int kKStages = 2, kVStages = 2;
 constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 constexpr unsigned long long kAttnWaitNs = 2000000000ull;
 constexpr int kMaxChunks = 16;
 
-// TMEM columns: O_i at 128*i; S_i buffer b (64 fp32 columns, later its P: 32 columns of bf16
-// pairs) at 256 + 128*i + 64*b.
-__host__ __device__ constexpr int col_o(int i) { return 128 * i; }
-__host__ __device__ constexpr int col_s(int i, int b) { return 256 + 128 * i + 64 * b; }
+// TMEM columns of query tile i: O_i at 256*i, S_i / P_i at 256*i + 128.
+__host__ __device__ constexpr int col_o(int i) { return 256 * i; }
+__host__ __device__ constexpr int col_s(int i) { return 256 * i + 128; }
 
 // Shared memory (from a 1024-byte aligned base): Q tiles | K stages | V stages | barriers.
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQTiles * kQTile;
-constexpr int kOffV = kOffK + kKStages * kKVTile;
-constexpr int kOffBar = kOffV + kVStages * kKVTile;
+constexpr int kOffK = kOffQ + kQTiles * kTile;
+constexpr int kOffV = kOffK + kKStages * kTile;
+constexpr int kOffBar = kOffV + kVStages * kTile;
 enum Bar {
   kQFull, kQEmpty, kKFull0, kKEmpty0 = kKFull0 + kKStages, kVFull0 = kKEmpty0 + kKStages,
-  kVEmpty0 = kVFull0 + kVStages,
-  kSFull0 = kVEmpty0 + kVStages,   // [query tile][buffer]
-  kPFull0 = kSFull0 + 2 * kQTiles,  // [query tile][buffer]
-  kPvDone0 = kPFull0 + 2 * kQTiles, // [query tile][buffer]
-  kMmaDone = kPvDone0 + 2 * kQTiles, kNumBars
+  kVEmpty0 = kVFull0 + kVStages, kSFull0 = kVEmpty0 + kVStages, kPFull0 = kSFull0 + kQTiles,
+  kOFinal0 = kPFull0 + kQTiles, kMmaDone = kOFinal0 + kQTiles, kNumBars
 };
 constexpr int kOffTmem = kOffBar + 8 * kNumBars;
 constexpr int kOffAbort = kOffTmem + 4;
@@ -127,19 +120,6 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Non-blocking test of phase `parity` (test_wait never suspends the thread, unlike try_wait,
-// which may park it for a while when the phase is incomplete: polling loops must not park).
-__device__ __forceinline__ bool bar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -164,32 +144,6 @@ __device__ __noinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile in
     }
   }
 }
-
-// Deadline of a polling loop: step(progressed) returns false once nothing progressed for
-// kAttnWaitNs (raising the abort flag, counted once by `count`) or the CTA aborted.  The
-// clock is read once per 64 idle rounds (a %globaltimer read is slow next to a try_wait).
-struct Poll {
-  unsigned long long since = 0;
-  unsigned idle = 0;
-  __device__ bool step(bool progressed, volatile int* abort_flag, bool count) {
-    if (progressed) {
-      idle = 0;
-      since = 0;
-      return true;
-    }
-    if ((++idle & 63) != 0) return true;
-    if (*abort_flag) return false;
-    const unsigned long long now = now_ns();
-    if (since == 0) {
-      since = now;
-    } else if (now - since > kAttnWaitNs) {
-      if (count) atomicAdd(&g_attn_timeouts, 1u);
-      *abort_flag = 1;
-      return false;
-    }
-    return true;
-  }
-};
 
 __device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
   asm volatile(
@@ -250,6 +204,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -257,27 +219,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x for x <= ~9 without the MUFU (range reduction plus a polynomial, the textbook method):
-// x = n + f with n = round(x) read from the low mantissa bits of x + 1.5*2^23 and f in
-// [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted here to 2^f on that
-// interval by iteratively reweighted least squares (relative error <= 7.5e-5, 26 times below
-// half a bf16 ulp); 2^n added to the exponent field.  x < -125 gives 0.
-__device__ __forceinline__ float exp2_poly(float x) {
-  const float xc = fmaxf(x, -125.f);
-  const float t = __fadd_rn(xc, 12582912.f);
-  const float f = __fsub_rn(xc, __fsub_rn(t, 12582912.f));
-  const float q = fmaf(fmaf(fmaf(0.055171236395835876f, f, 0.24261020123958588f), f, 0.6932609677314758f), f,
-                       0.9999281167984009f);
-  const float r = __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
-  return x < -125.f ? 0.f : r;
-}
-
-__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
-  f32x2 r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
 }
 
 // Shared-memory matrix descriptor of a 128-byte swizzled tile (sm_100 format: start address,
@@ -288,9 +229,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 }
 
 // Instruction descriptor of tcgen05.mma kind::f16: fp32 D, bf16 A and B, A K-major, B K-major
-// (b_mn = 0) or MN-major (b_mn = 1), M = 128, N = n.
-__host__ __device__ constexpr uint32_t mma_idesc(uint32_t b_mn, uint32_t n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn << 16) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+// (b_mn = 0) or MN-major (b_mn = 1), M = 128, N = 128.
+__host__ __device__ constexpr uint32_t mma_idesc(uint32_t b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -316,7 +257,6 @@ __device__ __forceinline__ void piece_of(const AParams& p, int64_t index, Piece&
   pc.index = index;
 }
 
-template <int EMU>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ AParams p) {
@@ -341,10 +281,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bar_init(bar(kVFull0 + s), 1);
       bar_init(bar(kVEmpty0 + s), 1);
     }
-    for (int i = 0; i < 2 * kQTiles; ++i) {
+    for (int i = 0; i < kQTiles; ++i) {
       bar_init(bar(kSFull0 + i), 1);
       bar_init(bar(kPFull0 + i), 128);      // every softmax thread of the tile
-      bar_init(bar(kPvDone0 + i), 1);
+      bar_init(bar(kOFinal0 + i), 1);
     }
     bar_init(bar(kMmaDone), 1);
     *abort_flag = 0;
@@ -367,7 +307,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto warp_wait = [&](int i, int parity) {
     return __all_sync(0xffffffffu, bar_wait(bar(i), parity, abort_flag, lane == 0));
   };
-  auto warp_try = [&](int i, int parity) { return __all_sync(0xffffffffu, bar_test(bar(i), parity)); };
   const bool leader = lane == 0;
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------
@@ -382,49 +321,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n_pieces > 0 && !(ok = warp_wait(kQEmpty, (n_pieces - 1) & 1))) break;
       const int col = pc.h * kD;
       if (leader) {
-        bar_expect_tx(bar(kQFull), pc.two ? 2 * kQTile : kQTile);
+        bar_expect_tx(bar(kQFull), pc.two ? 2 * kTile : kTile);
         for (int i = 0; i < (pc.two ? 2 : 1); ++i) {
           const int row = (2 * pc.qb + i) * kBM;
-          tma_load(sbase + kOffQ + i * kQTile, &tq, col, row, pc.b, bar(kQFull));
-          tma_load(sbase + kOffQ + i * kQTile + kQHalf, &tq, col + 64, row, pc.b, bar(kQFull));
+          tma_load(sbase + kOffQ + i * kTile, &tq, col, row, pc.b, bar(kQFull));
+          tma_load(sbase + kOffQ + i * kTile + kHalf, &tq, col + 64, row, pc.b, bar(kQFull));
         }
       }
       ++n_pieces;
-      // K and V tiles are issued independently as their stages free up.
-      int kt = t, vt = t;
-      const int end_t = t + (pc.j1 - pc.j0);
-      Poll poll;
-      while (kt < end_t || vt < end_t) {
-        bool progressed = false;
-        if (kt < end_t) {
-          const int sk = kt % kKStages;
-          if (kt < kKStages || warp_try(kKEmpty0 + sk, ((kt / kKStages) & 1) ^ 1)) {
-            const int row = (pc.j0 + (kt - t)) * kBN;
-            if (leader) {
-              bar_expect_tx(bar(kKFull0 + sk), kKVTile);
-              tma_load(sbase + kOffK + sk * kKVTile, &tk, col, row, pc.b, bar(kKFull0 + sk));
-              tma_load(sbase + kOffK + sk * kKVTile + kKVHalf, &tk, col + 64, row, pc.b, bar(kKFull0 + sk));
-            }
-            last_k[sk] = kt++;
-            progressed = true;
-          }
+      for (int j = pc.j0; j < pc.j1; ++j, ++t) {
+        const int sk = t % kKStages, sv = t % kVStages;
+        if (t >= kKStages && !(ok = warp_wait(kKEmpty0 + sk, ((t / kKStages) & 1) ^ 1))) break;
+        if (leader) {
+          bar_expect_tx(bar(kKFull0 + sk), kTile);
+          tma_load(sbase + kOffK + sk * kTile, &tk, col, j * kBN, pc.b, bar(kKFull0 + sk));
+          tma_load(sbase + kOffK + sk * kTile + kHalf, &tk, col + 64, j * kBN, pc.b, bar(kKFull0 + sk));
         }
-        if (vt < end_t) {
-          const int sv = vt % kVStages;
-          if (vt < kVStages || warp_try(kVEmpty0 + sv, ((vt / kVStages) & 1) ^ 1)) {
-            const int row = (pc.j0 + (vt - t)) * kBN;
-            if (leader) {
-              bar_expect_tx(bar(kVFull0 + sv), kKVTile);
-              tma_load(sbase + kOffV + sv * kKVTile, &tv, col, row, pc.b, bar(kVFull0 + sv));
-              tma_load(sbase + kOffV + sv * kKVTile + kKVHalf, &tv, col + 64, row, pc.b, bar(kVFull0 + sv));
-            }
-            last_v[sv] = vt++;
-            progressed = true;
-          }
+        last_k[sk] = t;
+        if (t >= kVStages && !(ok = warp_wait(kVEmpty0 + sv, ((t / kVStages) & 1) ^ 1))) break;
+        if (leader) {
+          bar_expect_tx(bar(kVFull0 + sv), kTile);
+          tma_load(sbase + kOffV + sv * kTile, &tv, col, j * kBN, pc.b, bar(kVFull0 + sv));
+          tma_load(sbase + kOffV + sv * kTile + kHalf, &tv, col + 64, j * kBN, pc.b, bar(kVFull0 + sv));
         }
-        if (!(ok = poll.step(progressed, abort_flag, leader))) break;
+        last_v[sv] = t;
       }
-      t = end_t;
     }
     // Every load issued must have landed before the CTA may exit (bounded as well).
     if (leader) {
@@ -438,84 +359,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
-    // Per query tile i two independent streams: S_i(x) = Q_i K(x)^T into S buffer x % 2 (the
-    // buffer P_i(x - 2) V(x - 2), issued earlier, has finished reading: tcgen05 MMAs of one
-    // thread complete in order), and P_i(x) V(x) once the softmax has written P_i(x).  S runs
-    // up to two key tiles ahead of P V, so each softmax warpgroup finds its next S ready.
-    const uint32_t id_s = mma_idesc(0, kBN), id_pv = mma_idesc(1, kD);
-    int t = 0, n_pieces = 0;
-    int s_cnt[kQTiles] = {0, 0}, pv_cnt[kQTiles] = {0, 0};  // S / P V issued per query tile (all pieces)
+    const uint32_t id_s = mma_idesc(0), id_pv = mma_idesc(1);
+    int t = 0, t1 = 0, n_pieces = 0;  // key tiles (all / with query tile 1), pieces
     bool ok = true;
     Piece pc;
+    // S_i = Q_i K^T of key tile tt (K stage tt % kKStages) into the S_i columns.
+    auto issue_s = [&](int i, int tt) {
+      const uint32_t qa = sbase + kOffQ + i * kTile, ka = sbase + kOffK + (tt % kKStages) * kTile;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+        tc_mma(tmem + col_s(i), smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), id_s, kk > 0);
+      }
+    };
+    // O_i (+)= P_i V of key tile tt: A = P_i from tensor memory (bf16 pairs packed in the S_i
+    // columns, 8 columns per 16 keys), B = V (MN-major: the head dim along the swizzled rows,
+    // its two 64-column halves 16 KB apart, 8-row key groups 1 KB apart).
+    auto issue_pv = [&](int i, int tt, bool first) {
+      const uint32_t va = sbase + kOffV + (tt % kVStages) * kTile;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, smem_desc(va + kk * 16 * 128, kHalf, 1024), id_pv,
+                  !(first && kk == 0));
+    };
     for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
       piece_of(p, index, pc);
       const int nq = pc.two ? 2 : 1;
       if (!(ok = warp_wait(kQFull, n_pieces & 1))) break;
       ++n_pieces;
-      const int end_t = t + (pc.j1 - pc.j0);
-      int s_next[kQTiles] = {t, nq == 2 ? t : end_t}, pv_next[kQTiles] = {t, nq == 2 ? t : end_t};
-      int k_rel = t, v_rel = t;
-      Poll poll;
-      while (pv_next[0] < end_t || pv_next[1] < end_t) {
-        bool progressed = false;
-#pragma unroll
-        for (int i = 0; i < kQTiles; ++i) {
-          // S_i of the next key tile, at most two ahead of P_i V.
-          const int sx = s_next[i];
-          if (sx < end_t && sx < pv_next[i] + 2 && warp_try(kKFull0 + sx % kKStages, (sx / kKStages) & 1)) {
-            tc_fence_after();
-            const int b = s_cnt[i] & 1;
-            if (leader) {
-              const uint32_t qa = sbase + kOffQ + i * kQTile, ka = sbase + kOffK + (sx % kKStages) * kKVTile;
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                tc_mma(tmem + col_s(i, b), smem_desc(qa + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024),
-                       smem_desc(ka + (kk >> 2) * kKVHalf + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
-              }
-              tc_commit(bar(kSFull0 + 2 * i + b));
-            }
-            s_next[i] = sx + 1;
-            ++s_cnt[i];
-            progressed = true;
-          }
-          // P_i V of the oldest key tile whose probabilities are written.
-          const int vx = pv_next[i];
-          if (vx < end_t && vx < s_next[i]) {
-            const int b = pv_cnt[i] & 1;
-            if (warp_try(kPFull0 + 2 * i + b, (pv_cnt[i] >> 1) & 1) &&
-                warp_try(kVFull0 + vx % kVStages, (vx / kVStages) & 1)) {
-              tc_fence_after();
-              if (leader) {
-                const uint32_t va = sbase + kOffV + (vx % kVStages) * kKVTile;
-                // A = P_i from tensor memory (bf16 pairs, 8 columns per 16 keys); B = V (MN-major:
-                // the head dim along the swizzled rows, the two 64-column halves 8 KB apart, 8-row
-                // key groups 1 KB apart).
-#pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk)
-                  tc_mma_ts(tmem + col_o(i), tmem + col_s(i, b) + kk * 8, smem_desc(va + kk * 16 * 128, kKVHalf, 1024),
-                            id_pv, !(vx == t && kk == 0));
-                tc_commit(bar(kPvDone0 + 2 * i + b));
-              }
-              pv_next[i] = vx + 1;
-              ++pv_cnt[i];
-              progressed = true;
-            }
-          }
+      // Prologue: S of the piece's first key tile for both query tiles.
+      if (!(ok = warp_wait(kKFull0 + t % kKStages, (t / kKStages) & 1))) break;
+      tc_fence_after();
+      if (leader) {
+        for (int i = 0; i < nq; ++i) {
+          issue_s(i, t);
+          tc_commit(bar(kSFull0 + i));
         }
-        // Release the K and V stages both query tiles are done with.
-        const int s_low = s_next[0] < s_next[1] ? s_next[0] : s_next[1];
-        const int pv_low = pv_next[0] < pv_next[1] ? pv_next[0] : pv_next[1];
-        if (leader) {
-          for (int x = k_rel; x < s_low; ++x) tc_commit(bar(kKEmpty0 + x % kKStages));
-          for (int x = v_rel; x < pv_low; ++x) tc_commit(bar(kVEmpty0 + x % kVStages));
-          if (k_rel < end_t && s_low >= end_t) tc_commit(bar(kQEmpty));  // every S of the piece issued
-        }
-        k_rel = s_low > k_rel ? s_low : k_rel;
-        v_rel = pv_low > v_rel ? pv_low : v_rel;
-        __syncwarp();
-        if (!(ok = poll.step(progressed, abort_flag, leader))) break;
+        tc_commit(bar(kKEmpty0 + t % kKStages));
       }
-      t = end_t;
+      __syncwarp();
+      const int n = pc.j1 - pc.j0;
+      for (int jj = 0; jj < n; ++jj, ++t) {
+        const bool more = jj + 1 < n;
+        // P_0 V for this key tile, then S_0 of the next one.
+        if (!(ok = warp_wait(kPFull0, t & 1))) break;  // query tile 0 takes part in every key tile
+        if (!(ok = warp_wait(kVFull0 + t % kVStages, (t / kVStages) & 1))) break;
+        tc_fence_after();
+        if (leader) {
+          issue_pv(0, t, jj == 0);
+          if (!more) tc_commit(bar(kOFinal0));
+        }
+        __syncwarp();
+        if (more && !(ok = warp_wait(kKFull0 + (t + 1) % kKStages, ((t + 1) / kKStages) & 1))) break;
+        tc_fence_after();
+        if (leader) {
+          if (more) {
+            issue_s(0, t + 1);
+            tc_commit(bar(kSFull0));
+          }
+          if (nq == 1) {
+            tc_commit(bar(kVEmpty0 + t % kVStages));
+            if (more) tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
+            else tc_commit(bar(kQEmpty));
+          }
+        }
+        __syncwarp();
+        if (nq == 2) {
+          if (!(ok = warp_wait(kPFull0 + 1, t1 & 1))) break;
+          ++t1;
+          tc_fence_after();
+          if (leader) {
+            issue_pv(1, t, jj == 0);
+            tc_commit(bar(kVEmpty0 + t % kVStages));
+            if (!more) {
+              tc_commit(bar(kOFinal0 + 1));
+              tc_commit(bar(kQEmpty));
+            } else {
+              issue_s(1, t + 1);
+              tc_commit(bar(kSFull0 + 1));
+              tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
+            }
+          }
+          __syncwarp();
+        }
+      }
     }
     if (leader) tc_commit(bar(kMmaDone));
     __syncwarp();
@@ -525,34 +452,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;               // the TMEM lanes this warp may access
     const int row = quarter * 32 + lane;        // query row of the tile = TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t o_addr = lane_addr + col_o(qi);
-    int n = 0;                                  // key tiles this warpgroup has processed (all pieces)
+    const uint32_t s_addr = lane_addr + col_s(qi), o_addr = lane_addr + col_o(qi);
+    int n_tiles = 0, n_pieces = 0;              // key tiles / pieces this warpgroup has processed
     bool ok = true;
     Piece pc;
     for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
       piece_of(p, index, pc);
       if (qi == 1 && !pc.two) continue;         // query tile 1 past Lq: nothing to do
       float m = -INFINITY, l = 0.f;
-      for (int j = pc.j0; j < pc.j1; ++j, ++n) {
-        const int b = n & 1;
-        const uint32_t s_addr = lane_addr + col_s(qi, b);
-        if (!(ok = warp_wait(kSFull0 + 2 * qi + b, (n >> 1) & 1))) break;
+      for (int j = pc.j0; j < pc.j1; ++j, ++n_tiles) {
+        if (!(ok = warp_wait(kSFull0 + qi, n_tiles & 1))) break;
         tc_fence_after();
-        uint32_t s[64];
-        tmem_ld32(s_addr, s);
-        tmem_ld32(s_addr + 32, s + 32);
+        uint32_t s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, s + 32 * c);
         tmem_wait_ld();
         const int valid = p.Lk - j * kBN;  // keys of this tile inside the window
         if (valid < kBN) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
+          for (int i = 0; i < 128; ++i)
             if (i >= valid) s[i] = __float_as_uint(-INFINITY);
         }
         float mx[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = __uint_as_float(s[e]);
 #pragma unroll
-        for (int i = 8; i < 64; i += 8)
+        for (int i = 8; i < 128; i += 8)
 #pragma unroll
           for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], __uint_as_float(s[i + e]));
         const float row_max =
@@ -565,39 +490,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= alpha;
           m = m_new;
         }
-        // Probabilities (bf16 pairs, even key in the low half) written back as P over the S
-        // columns already read: x = s * scale * log2(e) - m in packed fp32 pairs; 2^x on the
-        // MUFU, or for EMU of every 8 pairs by the polynomial (exp2_poly) on the FMA pipe.
-        const f32x2 sc2 = f2_make(p.scale_log2, p.scale_log2), nm2 = f2_make(-m, -m);
-        f32x2 ls0 = 0, ls1 = 0;
-        uint32_t pk[32];
+        // Probabilities (bf16 pairs, even key in the low half) over the S columns already read.
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          float x0, x1;
-          f2_split(f2_fma(f2_make(__uint_as_float(s[2 * c]), __uint_as_float(s[2 * c + 1])), sc2, nm2), x0, x1);
-          if ((c & 7) < EMU) {
-            x0 = exp2_poly(x0);
-            x1 = exp2_poly(x1);
-          } else {
-            x0 = fast_exp2(x0);
-            x1 = fast_exp2(x1);
+        for (int h = 0; h < 4; ++h) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float x0 = fast_exp2(fmaf(__uint_as_float(s[32 * h + 2 * c]), p.scale_log2, -m));
+            const float x1 = fast_exp2(fmaf(__uint_as_float(s[32 * h + 2 * c + 1]), p.scale_log2, -m));
+            ls[(c & 1) * 2] += x0;
+            ls[(c & 1) * 2 + 1] += x1;
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+            pk[c] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          if (c & 1) ls1 = f2_add(ls1, f2_make(x0, x1)); else ls0 = f2_add(ls0, f2_make(x0, x1));
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-          pk[c] = *reinterpret_cast<uint32_t*>(&h2);
+          tmem_st16(s_addr + 16 * h, pk);
         }
-        tmem_st32(s_addr, pk);
-        {
-          float a, bb, c, d;
-          f2_split(ls0, a, bb);
-          f2_split(ls1, c, d);
-          l += (a + bb) + (c + d);
-        }
-        // P_i V of the previous key tile has completed (its phase of the other buffer's barrier:
-        // every phase is waited for in order); O may then be brought to the new reference.
-        if (n > 0 && !(ok = warp_wait(kPvDone0 + 2 * qi + (b ^ 1), ((n - 1) >> 1) & 1))) break;
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        // O holds this piece's earlier tiles: bring it to the new reference.  P_i V of the
+        // previous tile has completed (the commit of S_i for this tile follows it).
         if (__any_sync(0xffffffffu, grow) && j > pc.j0) {
-          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -610,11 +522,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        bar_arrive(bar(kPFull0 + 2 * qi + b));
+        bar_arrive(bar(kPFull0 + qi));
       }
       if (!ok) break;
       // Epilogue of the piece: O once the piece's last P V has landed.
-      if (!(ok = warp_wait(kPvDone0 + 2 * qi + ((n - 1) & 1), ((n - 1) >> 1) & 1))) break;
+      if (!(ok = warp_wait(kOFinal0 + qi, n_pieces & 1))) break;
+      ++n_pieces;
       tc_fence_after();
       const int q_row = (2 * pc.qb + qi) * kBM + row;
       const bool live = q_row < p.Lq;
@@ -723,22 +636,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ AP
 // ---------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------
-// The compiled shares of exp2 taken by the polynomial (out of every 8 probability pairs).
-constexpr int kEmuChoices[] = {0, 2, 3};
-using AttnFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, AParams);
-static AttnFn attn_fn(int emu) {
-  switch (emu) {
-    case 0: return attention_kernel<0>;
-    case 2: return attention_kernel<2>;
-    case 3: return attention_kernel<3>;
-    default: return nullptr;
-  }
-}
-
 struct APlan {
   AParams params;
   int64_t ws_bytes;
-  int emu;  // probability pairs of every 8 whose exp2 the polynomial takes
 };
 
 static int sm_count_attn() {
@@ -761,10 +661,10 @@ static int check_rows(const void* ptr, int64_t member_stride, int64_t row_stride
   return PS_OK;
 }
 
-// Key chunks per unit: the S (1..16) with the least modelled time, in 64-key tile times of one
-// CTA: whole rounds of pieces (a piece = its key tiles + ~4 tiles of set-up and epilogue), and
-// with S > 1 the partial results: ~6 tile times for a CTA to write a piece's 128 KB, and the
-// combine pass reading them all (~4 MB per tile time over the whole GPU).
+// Key chunks per unit: the S (1..16) with the least modelled time, in key-tile times of one
+// CTA: whole rounds of pieces (a piece = its key tiles + ~2 tiles of set-up and epilogue), and
+// with S > 1 the partial results: ~3 tile times for a CTA to write a piece's 128 KB, and the
+// combine pass reading them all (~8 MB per tile time over the whole GPU).
 static int choose_chunks(int64_t units, int nkv, int max_ctas) {
   int best = 1;
   double best_cost = 0;
@@ -772,8 +672,8 @@ static int choose_chunks(int64_t units, int nkv, int max_ctas) {
     const int64_t pieces = units * c;
     const int64_t G = pieces < max_ctas ? pieces : max_ctas;
     const int64_t rounds = (pieces + G - 1) / G;
-    double cost = static_cast<double>(rounds) * ((nkv + c - 1) / c + 4);
-    if (c > 1) cost += 6.0 * rounds + static_cast<double>(pieces) * kQTiles * kBM * kD * 4 / 4.0e6;
+    double cost = static_cast<double>(rounds) * ((nkv + c - 1) / c + 2);
+    if (c > 1) cost += 3.0 * rounds + static_cast<double>(pieces) * kQTiles * kBM * kD * 4 / 8.0e6;
     if (c == 1 || cost < best_cost) {
       best = c;
       best_cost = cost;
@@ -823,9 +723,6 @@ static int build_attn(const ps_attn_args* a, APlan* plan, bool host_only) {
   p.out_member_stride = a->out_member_stride;
   p.out_row_stride = a->out_row_stride;
   plan->ws_bytes = workspace_bytes(p.pieces, chunks);
-  plan->emu = a->exp2_poly_share == 0 ? 2 : (a->exp2_poly_share < 0 ? 0 : a->exp2_poly_share);
-  if (!attn_fn(plan->emu)) return fail(PS_ERR_UNSUPPORTED, "exp2_poly_share=%d (0 = automatic, -1 = none, 2, 3)",
-                                       a->exp2_poly_share);
   if (!host_only || a->workspace) {
     if (plan->ws_bytes > 0 && (!a->workspace || a->workspace_bytes < plan->ws_bytes))
       return fail(PS_ERR_NULL, "workspace of %lld bytes needed (ps_attention_workspace), %lld given",
@@ -851,16 +748,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// {64 columns, box_rows rows, 1 member} boxes of a [members, rows, C] bf16 tensor, 128-byte swizzle;
+// {64 columns, 128 rows, 1 member} boxes of a [members, rows, C] bf16 tensor, 128-byte swizzle;
 // rows beyond `rows` read as zero.
 static int make_map(CUtensorMap* map, const void* base, int64_t C, int64_t rows, int B, int64_t row_stride,
-                    int64_t member_stride, int box_rows, const char* name) {
+                    int64_t member_stride, const char* name) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   if (!encode) return fail(PS_ERR_LAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(B)};
   const int64_t mstride = B > 1 ? member_stride : rows * row_stride;
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * 2), static_cast<cuuint64_t>(mstride * 2)};
-  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBM), 1};
   const cuuint32_t estride[3] = {1, 1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                             estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -869,18 +766,16 @@ static int make_map(CUtensorMap* map, const void* base, int64_t C, int64_t rows,
   return PS_OK;
 }
 
-static cudaError_t allow_attn_smem(AttnFn fn) {
-  static int done[64][4];
+static cudaError_t allow_attn_smem() {
+  static int done_dev[64];
   static std::mutex lock;
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
-  int k = 0;
-  while (k < 3 && attn_fn(kEmuChoices[k]) != fn) ++k;
   std::lock_guard<std::mutex> guard(lock);
-  if (dev >= 0 && dev < 64 && k < 3 && done[dev][k]) return cudaSuccess;
-  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (err == cudaSuccess && dev >= 0 && dev < 64 && k < 3) done[dev][k] = 1;
+  if (dev >= 0 && dev < 64 && done_dev[dev]) return cudaSuccess;
+  err = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (err == cudaSuccess && dev >= 0 && dev < 64) done_dev[dev] = 1;
   return err;
 }
 
@@ -913,15 +808,14 @@ extern "C" int32_t ps_ring_attention(const ps_attn_args* args, void* stream) {
   if (plan.params.units == 0) return PS_OK;
   const int64_t C = static_cast<int64_t>(args->heads) * ps::kD;
   CUtensorMap tq, tk, tv;
-  if ((rc = ps::make_map(&tq, args->q, C, args->q_tokens, args->batch, args->q_row_stride, args->q_member_stride, ps::kBM, "q")) ||
-      (rc = ps::make_map(&tk, args->k, C, args->kv_tokens, args->batch, args->k_row_stride, args->k_member_stride, ps::kBN, "k")) ||
-      (rc = ps::make_map(&tv, args->v, C, args->kv_tokens, args->batch, args->v_row_stride, args->v_member_stride, ps::kBN, "v")))
+  if ((rc = ps::make_map(&tq, args->q, C, args->q_tokens, args->batch, args->q_row_stride, args->q_member_stride, "q")) ||
+      (rc = ps::make_map(&tk, args->k, C, args->kv_tokens, args->batch, args->k_row_stride, args->k_member_stride, "k")) ||
+      (rc = ps::make_map(&tv, args->v, C, args->kv_tokens, args->batch, args->v_row_stride, args->v_member_stride, "v")))
     return rc;
-  const ps::AttnFn fn = ps::attn_fn(plan.emu);
-  cudaError_t err = ps::allow_attn_smem(fn);
+  cudaError_t err = ps::allow_attn_smem();
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "attention smem opt-in: %s", cudaGetErrorString(err));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  fn<<<plan.params.G, ps::kThreads, ps::kSmemBytes, s>>>(tq, tk, tv, plan.params);
+  ps::attention_kernel<<<plan.params.G, ps::kThreads, ps::kSmemBytes, s>>>(tq, tk, tv, plan.params);
   err = cudaGetLastError();
   if (err != cudaSuccess) return ps::fail(PS_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(err));
   if (plan.params.chunks > 1) {

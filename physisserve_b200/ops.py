@@ -618,16 +618,15 @@ def _member_rows(t: torch.Tensor, C: int, name: str):
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_tokens: int | None = None, *,
               heads: int, out: torch.Tensor | None = None, scale: float | None = None, ctas: int = 0,
-              key_chunks: int = 0, exp2_poly_share: int = 0,
-              workspace: torch.Tensor | None = None) -> torch.Tensor:
+              key_chunks: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Softmax attention of the query rows over the window rows ``[0, kv_tokens)`` of K and V
     (``ps_ring_attention``): ``F.scaled_dot_product_attention`` of models/wan.py:110 over the
     ring rows instead of a concatenated window (engine/kv_cache.py:51-56).
 
     ``q``: [B, Lq, C] (or [B, Lq, H, D]) bf16 token-major rows; ``k``/``v``: [B, rows, C] ring
     storage (rows >= kv_tokens, default all rows); returns ``out`` [B, Lq, C] (allocated if
-    not given).  head_dim 128.  ``ctas`` / ``key_chunks`` override the work split and
-    ``exp2_poly_share`` the exp2 pairs (of every 8) computed by polynomial (0 = automatic).  The scratch for the partial results of key chunks comes from ``workspace`` (a
+    not given).  head_dim 128.  ``ctas`` / ``key_chunks`` override the work split (0 =
+    automatic).  The scratch for the partial results of key chunks comes from ``workspace`` (a
     byte tensor of at least the bytes ``ps_attention_workspace`` reports) or is allocated.
     """
     if q.dtype is not torch.bfloat16 or k.dtype is not torch.bfloat16 or v.dtype is not torch.bfloat16:
@@ -645,7 +644,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_tokens: int 
         out = torch.empty(B, Lq, C, device=device, dtype=torch.bfloat16)
     qs, ks, vs, os_ = (_member_rows(t, C, n) for t, n in ((q, "q"), (k, "k"), (v, "v"), (out, "out")))
     args = _lib.PsAttnArgs(_lib.BF16, heads, C // heads, B, Lq, kv_tokens, float(scale or 0.0), int(ctas),
-                           int(key_chunks), int(exp2_poly_share), q.data_ptr(), *qs, k.data_ptr(), *ks, v.data_ptr(), *vs,
+                           int(key_chunks), 0, q.data_ptr(), *qs, k.data_ptr(), *ks, v.data_ptr(), *vs,
                            out.data_ptr(), *os_, None, 0)
     lib = _lib.load()
     with _on_device(device.index):

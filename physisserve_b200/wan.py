@@ -291,13 +291,14 @@ class RingAttention:
 
     ``cache`` is a ``RingCache`` (one per stream cell, set per block call like the
     reference's ``cache``) and ``rotary_emb`` is ``(freqs_cos, freqs_sin, RingPositions
-    per member)``.  The attention reads the window straight from the ring storage: the
-    sm_100a ring attention kernel (``ops.attention``) for bf16 with head_dim 128, torch SDPA
-    over the ring views otherwise.
+    per member)``.  The attention reads the window straight from the ring storage: torch SDPA
+    over the ring views (the reference's call, default), or with ``attention_kernel=True``
+    the sm_100a ring attention kernel (``ops.attention``, bf16 with head_dim 128).
     """
 
-    def __init__(self):
+    def __init__(self, attention_kernel: bool = False):
         self.cache = None
+        self.attention_kernel = attention_kernel
 
     def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, rotary_emb=None):
         freqs_cos, freqs_sin, positions = rotary_emb
@@ -311,7 +312,7 @@ class RingAttention:
         q_rot = prep_ring(q, k, v, _norm_weight(attn.norm_q, C, q.dtype, q.device),
                           _norm_weight(attn.norm_k, C, k.dtype, k.device), _norm_eps(attn.norm_q, q.dtype),
                           freqs_cos, freqs_sin, cache, positions)
-        if D == 128 and q.dtype == torch.bfloat16:
+        if self.attention_kernel and D == 128 and q.dtype == torch.bfloat16:
             # The ring attention kernel reads each member's window rows where the prep wrote them.
             windows = [cache.window_rows(pos.chunk) for pos in positions]
             if len(set(windows)) == 1:

@@ -80,15 +80,6 @@ def test_attention_matches_fp32_reference(B, Lq, rows, kv, heads, ctas, chunks):
     assert ops.attention_timeouts(reset=True) == 0
 
 
-@pytest.mark.parametrize("share", [-1, 2, 3])
-def test_attention_exp2_polynomial_shares(share):
-    """Every compiled share of exp2 computed by the polynomial instead of the MUFU."""
-    heads, B, Lq, kv = 2, 2, 300, 900
-    q, k, v = _inputs(B, Lq, kv, heads, seed=31)
-    got = ops.attention(q, k, v, kv, heads=heads, exp2_poly_share=share)
-    _check(got, q, k, v, heads, kv, f"exp2 polynomial share {share}/8")
-
-
 def test_attention_large_scores_rescale():
     """Scores that grow along the window (later keys dominate): the running max moves by far
     more than 2^8, so O is rescaled in tensor memory, and results still match."""

@@ -579,15 +579,17 @@ def test_prepare_reference_layout_batch_members(golden):
                          f"batch page {m}")
 
 
-def test_ring_attention_processor_output_matches_reference(golden):
+@pytest.mark.parametrize("attention_kernel", [False, True])
+def test_ring_attention_processor_output_matches_reference(golden, attention_kernel):
     """RingAttention over the recorded request: the block's attention output equals the
-    reference _Attention's (keys in ring order only change SDPA's summation order)."""
+    reference _Attention's (keys in ring order only change the summation order), with torch
+    SDPA over the ring views and with the sm_100a ring attention kernel."""
     g = golden("attention.pt")
     heads, D = g["heads"], g["head_dim"]
     gh, gw = g["grid"]
     attn = _attn(g)
     from physisserve_b200.wan import RingAttention
-    processor = RingAttention()
+    processor = RingAttention(attention_kernel=attention_kernel)
     processor.cache = RingCache(heads=heads, head_dim=D, grid_h=gh, grid_w=gw, device=DEV)
     cos, sin = g["freqs_cos"].to(DEV), g["freqs_sin"].to(DEV)
     records = {r["chunk"]: r for r in g["records"]}
