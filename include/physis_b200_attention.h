@@ -79,6 +79,29 @@ PS_API int32_t ps_ring_attention(const ps_attn_args* args, void* stream);
  * its outputs are undefined).  Synchronises the device first. */
 PS_API int32_t ps_attention_timeouts(uint32_t* count, int32_t reset);
 
+/* Bytes of the scratch array inside the library that ps_ring_attention_static
+ * uses: 32 MiB, held by every GPU that loads the library until the process exits. */
+#define PS_ATTN_STATIC_SCRATCH_BYTES (32u << 20)
+
+/* ps_ring_attention for callers that cannot give this library device memory.
+ * (No counterpart in the reference: PhysisServe lets torch allocate SDPA's
+ * scratch.)  Some hosts cannot allocate for it: a plain C or FFI host that only
+ * holds the tensors it passes in and has no device allocator to lend, or an
+ * engine that forbids device allocation once serving starts so that its memory
+ * stays fixed.  This entry point allocates nothing: args->workspace and
+ * args->workspace_bytes are ignored, and the partial results of key chunks go
+ * to the library's own PS_ATTN_STATIC_SCRATCH_BYTES array instead.
+ *
+ * With key_chunks 0 it takes the fastest split whose partial results fit that
+ * array (one key chunk needs none); an explicit key_chunks whose partial results
+ * need more returns PS_ERR_UNSUPPORTED.  The first call on a device looks up the
+ * array's device address there (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  All calls share the one array and it keeps the
+ * last call's contents (every value a call reads back it has written itself, so
+ * nothing needs clearing), so calls that overlap on the GPU -- on two streams, or
+ * from two threads -- race; order them on one stream. */
+PS_API int32_t ps_ring_attention_static(const ps_attn_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,11 +34,14 @@ ROPE_SPLIT, ROPE_INTERLEAVED = 0, 1
 LAUNCH_STREAM, LAUNCH_PDL, LAUNCH_PDL_EARLY_INPUTS = 0, 1, 2
 # ps_seq_kind
 SEQ_PREP, SEQ_SINK = 0, 1
+# PS_ATTN_STATIC_SCRATCH_BYTES (include/physis_b200_attention.h)
+ATTN_STATIC_SCRATCH_BYTES = 32 << 20
 
 EXPORTS = ("ps_abi_version", "ps_error_message", "ps_qk_prep_validate", "ps_qk_norm_rope_kv",
            "ps_device_timeouts", "ps_wait_selftest", "ps_rope", "ps_rope_validate",
            "ps_table_prep_validate", "ps_qk_norm_rope_tables", "ps_rope_tables", "ps_rope_tables_validate",
-           "ps_attention_workspace", "ps_attention_validate", "ps_ring_attention", "ps_attention_timeouts")
+           "ps_attention_workspace", "ps_attention_validate", "ps_ring_attention", "ps_attention_timeouts",
+           "ps_ring_attention_static")
 
 
 class PsSeq(ctypes.Structure):
@@ -206,6 +209,8 @@ def load() -> ctypes.CDLL:
     lib.ps_ring_attention.argtypes = [ctypes.c_void_p, ctypes.c_void_p]  # (const ps_attn_args*, stream)
     lib.ps_attention_workspace.restype = ctypes.c_int32
     lib.ps_attention_workspace.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]
+    lib.ps_ring_attention_static.restype = ctypes.c_int32
+    lib.ps_ring_attention_static.argtypes = [ctypes.c_void_p, ctypes.c_void_p]  # (const ps_attn_args*, stream)
     lib.ps_attention_timeouts.restype = ctypes.c_int32
     lib.ps_attention_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32]
     version = lib.ps_abi_version()

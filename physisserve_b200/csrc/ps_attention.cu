@@ -779,8 +779,83 @@ static cudaError_t allow_attn_smem() {
   return err;
 }
 
+// ---------------------------------------------------------------------------------------
+// ps_ring_attention_static: the partial results in a scratch array inside the library
+// ---------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_attn_scratch[PS_ATTN_STATIC_SCRATCH_BYTES];
+
+// Device address of g_attn_scratch on the current device, looked up once per device.
+static int static_scratch(void** ptr) {
+  static void* addr[256];
+  static bool known[256];
+  static std::mutex lock;
+  int dev = 0;
+  const cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return fail(PS_ERR_LAUNCH, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (dev < 0 || dev >= 256) return fail(PS_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> guard(lock);
+  if (!known[dev]) {
+    void* a = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&a, g_attn_scratch);
+    if (e != cudaSuccess) return fail(PS_ERR_LAUNCH, "address of the attention scratch array: %s", cudaGetErrorString(e));
+    addr[dev] = a;
+    known[dev] = true;
+  }
+  *ptr = addr[dev];
+  return PS_OK;
+}
+
+// The key chunks of the fastest modelled split (the model of choose_chunks) whose partial
+// results fit `cap` bytes.
+static int choose_chunks_within(int64_t units, int nkv, int max_ctas, int64_t cap) {
+  int best = 1;
+  double best_cost = 0;
+  for (int c = 1; c <= kMaxChunks && c <= nkv; ++c) {
+    const int64_t pieces = units * c;
+    if (workspace_bytes(pieces, c) > cap) continue;
+    const int64_t G = pieces < max_ctas ? pieces : max_ctas;
+    const int64_t rounds = (pieces + G - 1) / G;
+    double cost = static_cast<double>(rounds) * ((nkv + c - 1) / c + 2);
+    if (c > 1) cost += 3.0 * rounds + static_cast<double>(pieces) * kQTiles * kBM * kD * 4 / 8.0e6;
+    if (c == 1 || cost < best_cost) {
+      best = c;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 }  // namespace
 }  // namespace ps
+
+extern "C" int32_t ps_ring_attention_static(const ps_attn_args* args, void* stream) {
+  ps::clear_error();
+  if (!args) return ps::fail(PS_ERR_NULL, "args is NULL");
+  ps_attn_args a = *args;
+  if (a.q_tokens > 0 && a.head_dim == ps::kD && a.heads > 0 && a.batch > 0 && a.kv_tokens > 0) {
+    const int64_t qblocks = (static_cast<int64_t>(a.q_tokens) + ps::kQTiles * ps::kBM - 1) / (ps::kQTiles * ps::kBM);
+    const int64_t units = static_cast<int64_t>(a.batch) * a.heads * qblocks;
+    const int nkv = (a.kv_tokens + ps::kBN - 1) / ps::kBN;
+    const int max_ctas = a.ctas > 0 ? a.ctas : ps::sm_count_attn();
+    if (a.key_chunks == 0) {
+      a.key_chunks = ps::choose_chunks_within(units, nkv, max_ctas, PS_ATTN_STATIC_SCRATCH_BYTES);
+    } else {
+      const int chunks = a.key_chunks < nkv ? a.key_chunks : nkv;
+      const int64_t need = ps::workspace_bytes(units * chunks, chunks);
+      if (need > static_cast<int64_t>(PS_ATTN_STATIC_SCRATCH_BYTES))
+        return ps::fail(PS_ERR_UNSUPPORTED,
+                        "key_chunks=%d needs %lld bytes of scratch; the library's static scratch holds %u "
+                        "(use fewer key chunks, or ps_ring_attention with a workspace)",
+                        a.key_chunks, (long long)need, PS_ATTN_STATIC_SCRATCH_BYTES);
+    }
+  }
+  void* scratch = nullptr;
+  const int rc = ps::static_scratch(&scratch);
+  if (rc != PS_OK) return rc;
+  a.workspace = scratch;
+  a.workspace_bytes = PS_ATTN_STATIC_SCRATCH_BYTES;
+  return ps_ring_attention(&a, stream);
+}
 
 extern "C" int32_t ps_attention_workspace(const ps_attn_args* args, int64_t* bytes) {
   if (!bytes) return ps::fail(PS_ERR_NULL, "bytes is NULL");
