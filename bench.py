@@ -774,6 +774,23 @@ def run_pipeline(args):
     prep_tick_us = max_over_ranks(1000 * prep_ms / args.steps, world, device)
     timed_launches = launches[0]
 
+    # The handoff alone: the same two transfers per tick with no block launches, device-timed
+    # on the compute stream (each Pending.wait() makes it wait for the NCCL work).
+    probe = [initial[m] for m in ((0, 1) if stage == 0 else (2, 3))]
+    dist.barrier()
+    torch.cuda.synchronize()
+    begin.record(stream)
+    for t in range(args.steps):
+        for lane in range(2):
+            mine = ("x", rank, peer, item_spec, probe[lane])
+            theirs = ("y", peer, rank, item_spec, None)
+            got = transport.transfer([mine, theirs] if stage == 0 else [theirs, mine])
+            got["y"].wait()
+    finish.record(stream)
+    torch.cuda.synchronize()
+    transport.flush()
+    nccl_tick_us = max_over_ranks(1000 * begin.elapsed_time(finish) / args.steps, world, device)
+
     # Correctness: 8 ticks from the seeded start, then each stage holds its own two
     # micro-batches again, each through 4 x 30 blocks; compare with the serial run.
     lanes = fresh_lanes()
@@ -805,7 +822,9 @@ def run_pipeline(args):
                        "handoff_bytes_per_tick": 2 * (T * C * 2 + math.prod(latent_shape) * 2),
                        "step": "one pipeline tick", "launch": args.launch},
             "tick_us": tick_us, "prep_us_per_tick": prep_tick_us,
+            "nccl_us_per_tick": nccl_tick_us,
             "handoff_stall_us_per_tick": max(0.0, tick_us - prep_tick_us),
+            "overlap_us_per_tick": max(0.0, prep_tick_us + nccl_tick_us - tick_us),
             "check": "ok" if all(checks) else f"mismatch on ranks {[r for r, c in enumerate(checks) if not c]}",
             "clocks": {"per_rank": all_clocks, **all_clocks[0]},
             "gpu_launches": timed_launches, "e2e": None,
