@@ -120,6 +120,18 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of phase `parity` (no suspension, unlike try_wait).
+__device__ __forceinline__ bool bar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -304,7 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Every role runs its loop with the whole warp (the warp stays converged for the
   // .sync.aligned tensor-memory instructions and the final barrier); lane 0 issues the TMA
   // copies, MMAs and commits.  A warp-wide wait succeeds only if it succeeded on every lane.
-  auto warp_wait = [&](int i, int parity) {
+  // The phase waited for has often completed already (the MMA warp's operands arrive while it
+  // issues the previous step): a non-blocking test returns in a few cycles, where the blocking
+  // path (a call, try_wait) measured ~300 cycles even for a completed phase -- cycles in which
+  // the tensor core ran dry.
+  auto warp_wait = [&](int i, int parity) -> bool {
+    if (__all_sync(0xffffffffu, bar_test(bar(i), parity))) return true;
     return __all_sync(0xffffffffu, bar_wait(bar(i), parity, abort_flag, lane == 0));
   };
   const bool leader = lane == 0;
@@ -363,24 +380,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     int t = 0, t1 = 0, n_pieces = 0;  // key tiles (all / with query tile 1), pieces
     bool ok = true;
     Piece pc;
-    // S_i = Q_i K^T of key tile tt (K stage tt % kKStages) into the S_i columns.
+    // Descriptors of every Q tile and K / V stage, made once.  The eight K=16 steps of an MMA
+    // chain differ from its first descriptor by constant address offsets: the address field
+    // holds addr >> 4 and shared addresses stay below 2^18, so adding offset >> 4 cannot carry
+    // out of it.  The tensor core takes an M=128 N=128 K=16 step in ~64 cycles; any dependent
+    // work between issues (rebuilding a 64-bit descriptor) measured ~100 cycles per step on an
+    // SMSP shared with two softmax warps, so the chains below issue back to back.
+    // (Two of each: picked by a select, never by indexing a local array.)
+    static_assert(kQTiles == 2 && kKStages == 2 && kVStages == 2, "descriptor selects assume two of each");
+    const uint64_t q_desc0 = smem_desc(sbase + kOffQ, 16, 1024), q_desc1 = q_desc0 + (kTile >> 4);
+    const uint64_t k_desc0 = smem_desc(sbase + kOffK, 16, 1024), k_desc1 = k_desc0 + (kTile >> 4);
+    const uint64_t v_desc0 = smem_desc(sbase + kOffV, kHalf, 1024), v_desc1 = v_desc0 + (kTile >> 4);
+    // S_i = Q_i K^T of key tile tt (K stage tt % kKStages) into the S_i columns: step kk reads
+    // head-dim columns [16 kk, 16 kk + 16), 32 bytes into a 128-byte swizzled row, the second
+    // 64 columns in the other 16 KB half.
     auto issue_s = [&](int i, int tt) {
-      const uint32_t qa = sbase + kOffQ + i * kTile, ka = sbase + kOffK + (tt % kKStages) * kTile;
+      const uint64_t qd = i ? q_desc1 : q_desc0, kd = (tt & 1) ? k_desc1 : k_desc0;
+      const uint32_t d = tmem + col_s(i);
+      tc_mma(d, qd, kd, id_s, false);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-        tc_mma(tmem + col_s(i), smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), id_s, kk > 0);
+      for (int kk = 1; kk < 8; ++kk) {
+        const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4);
+        tc_mma(d, qd + off, kd + off, id_s, true);
       }
     };
     // O_i (+)= P_i V of key tile tt: A = P_i from tensor memory (bf16 pairs packed in the S_i
     // columns, 8 columns per 16 keys), B = V (MN-major: the head dim along the swizzled rows,
-    // its two 64-column halves 16 KB apart, 8-row key groups 1 KB apart).
+    // its two 64-column halves 16 KB apart, 8-row key groups 1 KB apart; step kk starts 16 key
+    // rows = 2 KB further).
     auto issue_pv = [&](int i, int tt, bool first) {
-      const uint32_t va = sbase + kOffV + (tt % kVStages) * kTile;
+      const uint64_t vd = (tt & 1) ? v_desc1 : v_desc0;
+      const uint32_t d = tmem + col_o(i), a = tmem + col_s(i);
+      tc_mma_ts(d, a, vd, id_pv, !first);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        tc_mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, smem_desc(va + kk * 16 * 128, kHalf, 1024), id_pv,
-                  !(first && kk == 0));
+      for (int kk = 1; kk < 8; ++kk) tc_mma_ts(d, a + kk * 8, vd + static_cast<uint64_t>(kk * 128), id_pv, true);
     };
     for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
       piece_of(p, index, pc);

@@ -217,15 +217,18 @@ def _window_positions(chunk, hw):
     return window, own
 
 
-@pytest.mark.parametrize("style", ["split", "interleaved"])
-def test_ltx_processors_over_a_request(style):
+@pytest.mark.parametrize("style,autocast", [("split", False), ("interleaved", False), ("split", True),
+                                            ("interleaved", True)])
+def test_ltx_processors_over_a_request(style, autocast):
+    """The reference runs every LTX block call under torch.autocast(cuda, bf16)
+    (ltx2.py:207/310/324/380); the processors are compared both outside and inside it."""
     B, H, D, hw = 2, 4, 32, 6
     C = H * D
     attn = _StubAttention(C, H, style, gated=True, seed=3).to(DEV, torch.bfloat16)
     ours, ref, ring = ltx.Attention(), oracle.Attention(), ltx.RingAttention()
     ring.cache = RingCache(heads=H, head_dim=D, grid_h=2, grid_w=3, batch=B, device=DEV)
     pages_ours, pages_ref = {}, {}
-    with torch.no_grad():
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
         for chunk in range(24):
             T = _frames(chunk) * hw
             hidden = randn((B, T, C), seed=1000 + chunk).to(DEV)
