@@ -422,6 +422,10 @@ class PrepPlan:
 
     def __init__(self, **kwargs):
         self.device_index, self.parts, self.signatures = _prepare(**kwargs)
+        # The packed arguments hold raw device pointers, so the plan owns every tensor they point
+        # at: an output passed as a temporary would otherwise be freed after this call and its
+        # memory handed to another tensor while every launch keeps writing there.
+        self._tensors = {name: t for name, t in kwargs.items() if isinstance(t, torch.Tensor)}
         self._lib = _lib.load()
 
     def launch(self, *, check_timeouts: bool = False, **tensors) -> None:
@@ -436,6 +440,7 @@ class PrepPlan:
             ptr = t.data_ptr()
             for args, _seq_buf in self.parts:
                 struct.pack_into("=Q", args, _FIELD_OFFSETS[name], ptr)
+            self._tensors[name] = t   # the packed pointer now names this tensor: keep it alive
         with _on_device(self.device_index):
             stream = _current_stream(self.device_index)
             for args, _seq_buf in self.parts:

@@ -339,3 +339,32 @@ def test_config5_full_shape_thirty_blocks_through_a_plan():
         _check_rows(slots_k.view(S * hw, C), ref_k.view(S * hw, C), ck.view(S * hw, C), wk, f"K ring block {block}")
         assert not bool(ring_k.view(S, capacity, hw * C)[~written].any()), "K written outside the streams' slots"
         assert not bool(ring_v.view(S, capacity, hw * C)[~written].any()), "V written outside the streams' slots"
+
+
+# ---------------------------------------------------------------------------------------
+# Launch plans own the tensors their packed pointers name
+# ---------------------------------------------------------------------------------------
+def test_plan_keeps_the_tensors_it_points_at():
+    """A PrepPlan packs raw device pointers, so outputs passed as temporaries must stay
+    allocated for the plan's lifetime: otherwise their memory goes to later tensors and every
+    launch writes into them (this corrupted a pipelined stage's hidden state)."""
+    import gc
+    import weakref
+
+    H, D, gh, gw = 2, 128, 4, 6
+    C, hw = H * D, gh * gw
+    g = torch.Generator().manual_seed(41)
+    q, k, v = (torch.randn(hw, C, generator=g).bfloat16().to(DEV) for _ in range(3))
+    cos, sin = (t.to(DEV) for t in oracle.rope_tables(D, 64))
+    ring_v = torch.zeros(2 * hw, C, device=DEV, dtype=torch.bfloat16)
+    watch = weakref.ref(ring_v)
+    plan = PrepPlan(heads=H, head_dim=D, seqs=[Seq(0, hw, gh, gw, 3, 0, 0, 2, 1)], cos=cos, sin=sin, q=q, k=k,
+                    v=v, q_out=torch.empty_like(q), k_out=torch.zeros_like(ring_v), v_out=ring_v)
+    del ring_v
+    gc.collect()
+    assert watch() is not None, "the plan let its V ring go"
+    fillers = [torch.full((2 * hw, C), 7.0, device=DEV, dtype=torch.bfloat16) for _ in range(8)]
+    plan.launch(q=q)
+    torch.cuda.synchronize()
+    assert all(bool((f == 7.0).all()) for f in fillers), "a launch wrote into a later tensor"
+    assert torch.equal(watch()[hw:2 * hw], v)       # slot 1 of the 2-frame ring holds V
