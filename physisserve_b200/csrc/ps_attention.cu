@@ -415,68 +415,70 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int kk = 1; kk < 8; ++kk) tc_mma_ts(d, a + kk * 8, vd + static_cast<uint64_t>(kk * 128), id_pv, true);
     };
-    for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
-      piece_of(p, index, pc);
-      const int nq = pc.two ? 2 : 1;
-      if (!(ok = warp_wait(kQFull, n_pieces & 1))) break;
-      ++n_pieces;
-      // Prologue: S of the piece's first key tile for both query tiles.
-      if (!(ok = warp_wait(kKFull0 + t % kKStages, (t / kKStages) & 1))) break;
-      tc_fence_after();
-      if (leader) {
+    // The loop runs on lane 0 alone.  The tensor core keeps almost no issued MMAs queued, so
+    // the gaps between chains are tensor-pipe idle time: a warp-wide barrier test, reconvergence
+    // and __syncwarp between chains measured ~14 cycles per MMA more than back-to-back issue
+    // (78 against 64), and ~25 more inside this kernel.  A single thread waits with plain
+    // barrier tests and goes straight on to the next chain.
+    auto wait1 = [&](int i, int parity) -> bool {
+      return bar_test(bar(i), parity) || bar_wait(bar(i), parity, abort_flag, true);
+    };
+    if (leader) {
+      for (int64_t index = blockIdx.x; ok && index < p.pieces; index += p.G) {
+        piece_of(p, index, pc);
+        const int nq = pc.two ? 2 : 1;
+        if (!(ok = wait1(kQFull, n_pieces & 1))) break;
+        ++n_pieces;
+        // Prologue: S of the piece's first key tile for both query tiles.
+        if (!(ok = wait1(kKFull0 + t % kKStages, (t / kKStages) & 1))) break;
+        tc_fence_after();
         for (int i = 0; i < nq; ++i) {
           issue_s(i, t);
           tc_commit(bar(kSFull0 + i));
         }
         tc_commit(bar(kKEmpty0 + t % kKStages));
-      }
-      __syncwarp();
-      const int n = pc.j1 - pc.j0;
-      for (int jj = 0; jj < n; ++jj, ++t) {
-        const bool more = jj + 1 < n;
-        // P_0 V for this key tile, then S_0 of the next one.
-        if (!(ok = warp_wait(kPFull0, t & 1))) break;  // query tile 0 takes part in every key tile
-        if (!(ok = warp_wait(kVFull0 + t % kVStages, (t / kVStages) & 1))) break;
-        tc_fence_after();
-        if (leader) {
+        const int n = pc.j1 - pc.j0;
+        for (int jj = 0; jj < n; ++jj, ++t) {
+          const bool more = jj + 1 < n;
+          // The loads of V(t) and K(t+1) landed long ago (two-stage rings): test them first, so
+          // that PV0(t) -> S0(t+1) and PV1(t) -> S1(t+1) issue back to back and the only waits
+          // between chains are for the softmax warps' probabilities.
+          if (!(ok = wait1(kVFull0 + t % kVStages, (t / kVStages) & 1))) break;
+          if (more && !(ok = wait1(kKFull0 + (t + 1) % kKStages, ((t + 1) / kKStages) & 1))) break;
+          // P_0 V for this key tile, then S_0 of the next one.
+          if (!(ok = wait1(kPFull0, t & 1))) break;  // query tile 0 takes part in every key tile
+          tc_fence_after();
           issue_pv(0, t, jj == 0);
-          if (!more) tc_commit(bar(kOFinal0));
-        }
-        __syncwarp();
-        if (more && !(ok = warp_wait(kKFull0 + (t + 1) % kKStages, ((t + 1) / kKStages) & 1))) break;
-        tc_fence_after();
-        if (leader) {
           if (more) {
             issue_s(0, t + 1);
             tc_commit(bar(kSFull0));
+          } else {
+            tc_commit(bar(kOFinal0));
           }
           if (nq == 1) {
             tc_commit(bar(kVEmpty0 + t % kVStages));
             if (more) tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
             else tc_commit(bar(kQEmpty));
-          }
-        }
-        __syncwarp();
-        if (nq == 2) {
-          if (!(ok = warp_wait(kPFull0 + 1, t1 & 1))) break;
-          ++t1;
-          tc_fence_after();
-          if (leader) {
+          } else {
+            if (!(ok = wait1(kPFull0 + 1, t1 & 1))) break;
+            ++t1;
+            tc_fence_after();
             issue_pv(1, t, jj == 0);
-            tc_commit(bar(kVEmpty0 + t % kVStages));
             if (!more) {
+              tc_commit(bar(kVEmpty0 + t % kVStages));
               tc_commit(bar(kOFinal0 + 1));
               tc_commit(bar(kQEmpty));
             } else {
               issue_s(1, t + 1);
+              tc_commit(bar(kVEmpty0 + t % kVStages));
               tc_commit(bar(kSFull0 + 1));
               tc_commit(bar(kKEmpty0 + (t + 1) % kKStages));
             }
           }
-          __syncwarp();
         }
       }
     }
+    __syncwarp();
     if (leader) tc_commit(bar(kMmaDone));
     __syncwarp();
   } else {
