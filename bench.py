@@ -674,7 +674,11 @@ def run_pipeline(args):
     C, hw = heads * D, gh * gw
     stage = layout.stage_of(rank)
     peer = layout.peer(rank, 1)
-    streams = layout.streams(spec["streams"], rank)
+    n_streams = args.streams or spec["streams"]
+    if n_streams % (4 * layout.pipelines):
+        raise SystemExit(f"--pipeline needs the stream count ({n_streams}) to split into 4 micro-batches "
+                         f"on each of {layout.pipelines} pipelines")
+    streams = layout.streams(n_streams, rank)
     micro = [streams[m::4] for m in range(4)]   # micro-batches 0, 1 start on stage 0; 2, 3 on stage 1
     T = len(micro[0]) * hw
     all_blocks = 30
@@ -718,6 +722,40 @@ def run_pipeline(args):
             src = out
         return out
 
+    # --graph: each micro-batch's pass through this stage's blocks is one CUDA graph over static
+    # buffers (the received hidden state is copied in, the result copied out by the send's
+    # packing), so a tick costs the host two graph launches instead of 30 plan launches.
+    stage_graphs, static = {}, {}
+    if args.graph:
+        for m in range(4):
+            s_in = torch.empty((T, C), device=device, dtype=torch.bfloat16)
+            s_out = torch.empty_like(s_in)
+            static[m] = (s_in, s_out)
+            s_in.copy_(initial[m][0])
+            src = s_in                      # one eager pass first: kernels loaded, plans warm
+            for b in blocks:
+                plans[m].launch(q=src, q_out=s_out, q_weight=wq[b], k_weight=wk[b])
+                src = s_out
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                src = s_in
+                for b in blocks:
+                    plans[m].launch(q=src, q_out=s_out, q_weight=wq[b], k_weight=wk[b])
+                    src = s_out
+            stage_graphs[m] = graph
+        torch.cuda.synchronize()
+
+    def run_stage(m, hidden):
+        """This stage's blocks on micro-batch m (a graph replay with --graph)."""
+        if not stage_graphs:
+            return run_blocks(m, hidden, blocks)
+        s_in, s_out = static[m]
+        s_in.copy_(hidden)
+        stage_graphs[m].replay()
+        launches[0] += len(blocks)
+        return s_out
+
     def fresh_lanes():
         # lane -> (micro-batch id, Pending of its (hidden, latent))
         from physisserve_b200.parallel import Pending
@@ -731,7 +769,7 @@ def run_pipeline(args):
             hidden, latent = pending.wait()
             if events is not None:
                 events[t][lane][0].record(stream)
-            out = run_blocks(m, hidden, blocks)
+            out = run_stage(m, hidden)
             if events is not None:
                 events[t][lane][1].record(stream)
             # Lane `lane` of this stage goes to the peer; the peer's same lane comes back.
@@ -816,11 +854,11 @@ def run_pipeline(args):
             "metric": "rotated_qk_tokens_per_s", "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": "cfg5-pipelined", "desc": "64 streams, 2-stage pipelines x 15 blocks, 2 lanes "
+            "config": {"workload": "cfg5-pipelined", "desc": f"{n_streams} streams, 2-stage pipelines x 15 blocks, 2 lanes "
                        "per stage; hidden state [tokens, 1536] bf16 + latent as one NCCL message per lane per tick",
                        "pipelines": layout.pipelines, "tokens_per_lane": T, "streams_per_lane": len(micro[0]),
                        "handoff_bytes_per_tick": 2 * (T * C * 2 + math.prod(latent_shape) * 2),
-                       "step": "one pipeline tick", "launch": args.launch},
+                       "step": "one pipeline tick", "launch": args.launch, "cuda_graph": bool(args.graph)},
             "tick_us": tick_us, "prep_us_per_tick": prep_tick_us,
             "nccl_us_per_tick": nccl_tick_us,
             "handoff_stall_us_per_tick": max(0.0, tick_us - prep_tick_us),
@@ -830,6 +868,7 @@ def run_pipeline(args):
             "gpu_launches": timed_launches, "e2e": None,
         }
         emit(line)
+    stage_graphs.clear()
     dist.destroy_process_group()
     return 0
 
@@ -1009,7 +1048,7 @@ def run_processor(args):
         drop_in.cache = Cache(pages)
         return drop_in(attn, hidden, rotary_emb=(own, window))
 
-    ring = RingAttention()
+    ring = RingAttention(attention_kernel=False)   # torch SDPA over the ring views
     ring.cache = RingCache(heads=H, head_dim=D, grid_h=gh, grid_w=gw, device=device)
     ring.cache.k.normal_()
     ring.cache.v.normal_()
@@ -1036,7 +1075,8 @@ def run_processor(args):
             torch.cuda.synchronize()
             results[name] = begin.elapsed_time(finish) / args.steps
     emit({"impl": "processor", "metric": "block_call_ms", "unit": "ms", "higher_is_better": False,
-          "value": results["ring"], "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+          "value": results["ring_attention_kernel"], "default_processor": "ring_attention_kernel",
+          "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
           "config": {"workload": "wan2.1-1.3b self-attention block call, chunk 25 (22-frame window)",
                      "tokens": hw, "window_tokens": 22 * hw},
           "ms_per_call": results, "speedup_vs_torch": {k: results["torch"] / v for k, v in results.items()},
@@ -1342,7 +1382,7 @@ def run_attention(args):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    H, D, Lq, Lk = 12, 128, 1560, 22 * 1560
+    H, D, Lq, Lk = args.attn_heads, 128, 1560, 22 * 1560
     B = args.attn_batch
     C = H * D
     g = torch.Generator().manual_seed(13)
@@ -1372,8 +1412,9 @@ def run_attention(args):
     peak = float(peaks["bf16_tflops"])
     emit({"impl": "attention", "metric": "attention_tflops", "unit": "TFLOP/s",
           "value": flops / (times["ours"] * 1e-6) / 1e12, "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
-          "config": {"workload": f"wan2.1-1.3b block-call attention, {B} member(s) x 1560 queries x 12 heads over "
-                                 "a 34 320-row ring window, bf16, head_dim 128", "flops_per_call": flops},
+          "config": {"workload": f"{'wan2.1-14b' if H == 40 else 'wan2.1-1.3b' if H == 12 else f'{H}-head'} block-call "
+                                 f"attention, {B} member(s) x 1560 queries x {H} heads over a 34 320-row ring window, "
+                                 "bf16, head_dim 128", "flops_per_call": flops},
           "us_per_call": times,
           "tflops": {name: flops / (t * 1e-6) / 1e12 for name, t in times.items()},
           "roofline": {"bound": "tensor", "peak": peak, "unit": "TFLOP/s", "peak_source": "MEASURED_PEAKS.json "
@@ -1523,6 +1564,7 @@ def main(argv=None):
     parser.add_argument("--attention", action="store_true",
                         help="time the ring attention kernel against torch SDPA on the 1.3B block-call window")
     parser.add_argument("--attn-batch", type=int, default=1, help="members of the --attention call")
+    parser.add_argument("--attn-heads", type=int, default=12, help="heads of the --attention call (12: Wan2.1-1.3B, 40: 14B)")
     parser.add_argument("--pipeline", action="store_true",
                         help="BASELINE config 5 pipelined: 2-stage pipelines (15 blocks per GPU) over NCCL")
     args = parser.parse_args(argv)
