@@ -241,7 +241,7 @@ class ClockSampler:
 # --------------------------------------------------------------------------------------
 # Distributed helpers
 # --------------------------------------------------------------------------------------
-def init_dist():
+def init_dist(high_priority_nccl=False):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -251,8 +251,15 @@ def init_dist():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        kwargs = {}
+        if high_priority_nccl:
+            # NCCL's kernels on a high-priority stream: the block scheduler then places their
+            # CTAs ahead of queued prep CTAs of the compute stream.
+            options = dist.ProcessGroupNCCL.Options()
+            options.is_high_priority_stream = True
+            kwargs["pg_options"] = options
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), **kwargs)
     return rank, world, local
 
 
@@ -646,7 +653,8 @@ def run_pipeline(args):
 
     Ranks form pipelines of two consecutive ranks (StageEqual's contiguous split of the 30
     blocks, engine/strategies/stage_equal.py:21-57); the 64 streams are sharded over
-    pipelines and each pipeline's streams split into 4 micro-batches, two per stage ("lanes").
+    pipelines and each pipeline's streams split into 2 x `--lanes` micro-batches, `--lanes` per
+    stage (default two).
     Each tick a stage runs its 15 blocks on lane 0 (one fused prep launch per block, Q taken
     from the hidden state), posts lane 0's handoff to the other stage, then runs lane 1 while
     lane 0's hidden state and latent are in flight, and posts lane 1's.  A lane waits for its
@@ -662,7 +670,7 @@ def run_pipeline(args):
     from physisserve_b200.parallel import PipelineLayout, Transport, stage_blocks
     from physisserve_b200.wan import wan_rope_tables
 
-    rank, world, local = init_dist()
+    rank, world, local = init_dist(high_priority_nccl=args.nccl_high_priority)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world < 2 or world % 2:
@@ -675,11 +683,13 @@ def run_pipeline(args):
     stage = layout.stage_of(rank)
     peer = layout.peer(rank, 1)
     n_streams = args.streams or spec["streams"]
-    if n_streams % (4 * layout.pipelines):
-        raise SystemExit(f"--pipeline needs the stream count ({n_streams}) to split into 4 micro-batches "
+    L = args.lanes
+    if n_streams % (2 * L * layout.pipelines):
+        raise SystemExit(f"--pipeline needs the stream count ({n_streams}) to split into {2 * L} micro-batches "
                          f"on each of {layout.pipelines} pipelines")
     streams = layout.streams(n_streams, rank)
-    micro = [streams[m::4] for m in range(4)]   # micro-batches 0, 1 start on stage 0; 2, 3 on stage 1
+    # micro-batches 0 .. L-1 start on stage 0, L .. 2L-1 on stage 1
+    micro = [streams[m::2 * L] for m in range(2 * L)]
     T = len(micro[0]) * hw
     all_blocks = 30
     blocks = list(stage_blocks(stage, 2, all_blocks))
@@ -708,7 +718,19 @@ def run_pipeline(args):
                               q_weight=wq[0], k_weight=wk[0], eps=1e-6, q_out=torch.empty_like(q0),
                               k_out=ring_k, v_out=torch.zeros_like(ring_k), launch=args.launch))
         initial.append((q0, seeded(500 + m, latent_shape)))
-    transport = Transport(device)
+    # One 2-rank NCCL communicator per pipeline (every rank creates every group, in the same
+    # order): with all ranks in one communicator NCCL spreads its point-to-point channels over
+    # all peers, and the 8-GPU handoff measured 2-3x slower than a pair's own communicator.
+    group = None
+    if not args.global_group:
+        options = None
+        if args.nccl_high_priority:
+            options = dist.ProcessGroupNCCL.Options()
+            options.is_high_priority_stream = True
+        groups = [dist.new_group(list(range(q * 2, q * 2 + 2)), pg_options=options) for q in range(layout.pipelines)]
+        group = groups[layout.pipeline_of(rank)]
+    me, other_stage = (stage, 1 - stage) if group is not None else (rank, peer)   # ranks as the group numbers them
+    transport = Transport(device, group=group)
     item_spec = [((T, C), torch.bfloat16), (latent_shape, torch.bfloat16)]
     launches = [0]
     stream = torch.cuda.current_stream(device)
@@ -727,7 +749,7 @@ def run_pipeline(args):
     # packing), so a tick costs the host two graph launches instead of 30 plan launches.
     stage_graphs, static = {}, {}
     if args.graph:
-        for m in range(4):
+        for m in range(2 * L):
             s_in = torch.empty((T, C), device=device, dtype=torch.bfloat16)
             s_out = torch.empty_like(s_in)
             static[m] = (s_in, s_out)
@@ -760,7 +782,7 @@ def run_pipeline(args):
         # lane -> (micro-batch id, Pending of its (hidden, latent))
         from physisserve_b200.parallel import Pending
 
-        own = (0, 1) if stage == 0 else (2, 3)
+        own = range(L) if stage == 0 else range(L, 2 * L)
         return [(m, Pending(initial[m])) for m in own]
 
     def tick(lanes, t, events=None):
@@ -774,10 +796,10 @@ def run_pipeline(args):
                 events[t][lane][1].record(stream)
             # Lane `lane` of this stage goes to the peer; the peer's same lane comes back.
             # Both ranks list the two items in the same (stage 0's item first) order.
-            # Lane L holds micro-batch L or L + 2 on either stage, the other one on the peer.
-            other = (m + 2) % 4
-            mine = ("x", rank, peer, item_spec, (out, latent))
-            theirs = ("y", peer, rank, item_spec, None)
+            # Lane l holds micro-batch l or l + L on either stage, the other one on the peer.
+            other = (m + L) % (2 * L)
+            mine = ("x", me, other_stage, item_spec, (out, latent))
+            theirs = ("y", other_stage, me, item_spec, None)
             got = transport.transfer([mine, theirs] if stage == 0 else [theirs, mine])
             new_lanes.append((other, got["y"]))
         return new_lanes
@@ -790,38 +812,41 @@ def run_pipeline(args):
     transport.flush()
     torch.cuda.synchronize()
     dist.barrier()
-    events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(2)] for _ in range(args.steps)]
+    events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)] for _ in range(args.steps)]
     begin, finish = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     launches[0] = 0
     torch.cuda.synchronize()
     sampler.start()
     begin.record(stream)
+    host0 = time.perf_counter()
     for t in range(args.steps):
         lanes = tick(lanes, t, events)
     for _, pending in lanes:
         pending.wait()
     finish.record(stream)
+    host_s = time.perf_counter() - host0     # the host's enqueue time (a host-bound run: ~ the tick)
     torch.cuda.synchronize()
     clocks = sampler.stop()
     transport.flush()
     dist.barrier()
     local_ms = begin.elapsed_time(finish)
-    prep_ms = sum(events[t][lane][0].elapsed_time(events[t][lane][1]) for t in range(args.steps) for lane in range(2))
+    prep_ms = sum(events[t][lane][0].elapsed_time(events[t][lane][1]) for t in range(args.steps) for lane in range(L))
     ms = max_over_ranks(local_ms, world, device)
     prep_tick_us = max_over_ranks(1000 * prep_ms / args.steps, world, device)
+    host_tick_us = max_over_ranks(1e6 * host_s / args.steps, world, device)
     timed_launches = launches[0]
 
     # The handoff alone: the same two transfers per tick with no block launches, device-timed
     # on the compute stream (each Pending.wait() makes it wait for the NCCL work).
-    probe = [initial[m] for m in ((0, 1) if stage == 0 else (2, 3))]
+    probe = [initial[m] for m in (range(L) if stage == 0 else range(L, 2 * L))]
     dist.barrier()
     torch.cuda.synchronize()
     begin.record(stream)
     for t in range(args.steps):
-        for lane in range(2):
-            mine = ("x", rank, peer, item_spec, probe[lane])
-            theirs = ("y", peer, rank, item_spec, None)
+        for lane in range(L):
+            mine = ("x", me, other_stage, item_spec, probe[lane])
+            theirs = ("y", other_stage, me, item_spec, None)
             got = transport.transfer([mine, theirs] if stage == 0 else [theirs, mine])
             got["y"].wait()
     finish.record(stream)
@@ -839,14 +864,14 @@ def run_pipeline(args):
     torch.cuda.synchronize()
     ok = True
     for m, got in finals.items():
-        order = list(range(all_blocks)) if m < 2 else [*range(15, all_blocks), *range(15)]
+        order = list(range(all_blocks)) if m < L else [*range(15, all_blocks), *range(15)]
         h = initial[m][0]
         for _ in range(4):
             h = run_blocks(m, h, order)
         ok = ok and bool(torch.equal(got, h))
     torch.cuda.synchronize()
     checks = gather_objects(ok, world)
-    tokens = sum(gather_objects(2 * T * len(blocks) * args.steps, world))
+    tokens = sum(gather_objects(L * T * len(blocks) * args.steps, world))
     all_clocks = gather_objects(clocks, world)
     if rank == 0:
         tick_us = 1000 * ms / args.steps
@@ -854,13 +879,15 @@ def run_pipeline(args):
             "metric": "rotated_qk_tokens_per_s", "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": "cfg5-pipelined", "desc": f"{n_streams} streams, 2-stage pipelines x 15 blocks, 2 lanes "
+            "config": {"workload": "cfg5-pipelined", "desc": f"{n_streams} streams, 2-stage pipelines x 15 blocks, {L} lane(s) "
                        "per stage; hidden state [tokens, 1536] bf16 + latent as one NCCL message per lane per tick",
                        "pipelines": layout.pipelines, "tokens_per_lane": T, "streams_per_lane": len(micro[0]),
-                       "handoff_bytes_per_tick": 2 * (T * C * 2 + math.prod(latent_shape) * 2),
-                       "step": "one pipeline tick", "launch": args.launch, "cuda_graph": bool(args.graph)},
+                       "handoff_bytes_per_tick": L * (T * C * 2 + math.prod(latent_shape) * 2),
+                       "step": "one pipeline tick", "lanes_per_stage": L, "launch": args.launch, "cuda_graph": bool(args.graph),
+                       "nccl_high_priority_stream": bool(args.nccl_high_priority),
+                       "communicator": "global" if group is None else "one per 2-rank pipeline"},
             "tick_us": tick_us, "prep_us_per_tick": prep_tick_us,
-            "nccl_us_per_tick": nccl_tick_us,
+            "nccl_us_per_tick": nccl_tick_us, "host_enqueue_us_per_tick": host_tick_us,
             "handoff_stall_us_per_tick": max(0.0, tick_us - prep_tick_us),
             "overlap_us_per_tick": max(0.0, prep_tick_us + nccl_tick_us - tick_us),
             "check": "ok" if all(checks) else f"mismatch on ranks {[r for r, c in enumerate(checks) if not c]}",
@@ -1564,6 +1591,12 @@ def main(argv=None):
     parser.add_argument("--attention", action="store_true",
                         help="time the ring attention kernel against torch SDPA on the 1.3B block-call window")
     parser.add_argument("--attn-batch", type=int, default=1, help="members of the --attention call")
+    parser.add_argument("--lanes", type=int, default=2, choices=(1, 2, 3, 4),
+                        help="--pipeline: micro-batches per stage (lane l's handoff overlaps lane l+1's blocks)")
+    parser.add_argument("--global-group", action="store_true",
+                        help="--pipeline: handoffs over the global communicator instead of one per pipeline")
+    parser.add_argument("--nccl-high-priority", action="store_true",
+                        help="--pipeline: NCCL on a high-priority stream (its CTAs ahead of queued prep CTAs)")
     parser.add_argument("--attn-heads", type=int, default=12, help="heads of the --attention call (12: Wan2.1-1.3B, 40: 14B)")
     parser.add_argument("--pipeline", action="store_true",
                         help="BASELINE config 5 pipelined: 2-stage pipelines (15 blocks per GPU) over NCCL")
