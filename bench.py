@@ -182,9 +182,13 @@ _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_
 
 
 class ClockSampler:
-    """Samples this rank's GPU SM clock, power and clock-event reasons with NVML in a thread."""
+    """Samples this rank's GPU SM clock, power and clock-event reasons with NVML in a thread:
+    once at start, every ``period_s``, once at stop.  A sample costs milliseconds of NVML time
+    and NVML calls contend with CUDA calls of every process on the host: at a 2 ms period,
+    8 ranks' samplers doubled the 8-GPU pipeline's tick (host enqueue time = the tick), so the
+    period is 50 ms and power is read on every fourth sample only."""
 
-    def __init__(self, device_index, period_s=0.002):
+    def __init__(self, device_index, period_s=0.05):
         self.period = period_s
         self.samples = []
         self.ok = False
@@ -203,20 +207,22 @@ class ClockSampler:
         self._stop = threading.Event()
         self._thread = None
 
-    def _sample(self):
+    def _sample(self, power=True):
         n = self.nvml
         sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
         try:
             reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
         except AttributeError:
             reasons = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
-        power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
-        self.samples.append((sm, reasons, power))
+        watts = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0 if power else None
+        self.samples.append((sm, reasons, watts))
 
     def _loop(self):
+        i = 0
         while not self._stop.is_set():
-            self._sample()
-            time.sleep(self.period)
+            self._sample(power=i % 4 == 0)
+            i += 1
+            self._stop.wait(self.period)
 
     def start(self):
         if self.ok:
@@ -235,7 +241,7 @@ class ClockSampler:
             mask |= s[1]
         reasons = [name for bit, name in _REASONS.items() if mask & bit]
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(sm), "power_w_max": max(s[2] for s in self.samples)}
+                "samples": len(sm), "power_w_max": max(s[2] for s in self.samples if s[2] is not None)}
 
 
 # --------------------------------------------------------------------------------------
