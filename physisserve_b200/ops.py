@@ -623,7 +623,8 @@ def _member_rows(t: torch.Tensor, C: int, name: str):
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_tokens: int | None = None, *,
               heads: int, out: torch.Tensor | None = None, scale: float | None = None, ctas: int = 0,
-              key_chunks: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+              key_chunks: int = 0, workspace: torch.Tensor | None = None,
+              check_timeouts: bool = False) -> torch.Tensor:
     """Softmax attention of the query rows over the window rows ``[0, kv_tokens)`` of K and V
     (``ps_ring_attention``): ``F.scaled_dot_product_attention`` of models/wan.py:110 over the
     ring rows instead of a concatenated window (engine/kv_cache.py:51-56).
@@ -633,6 +634,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_tokens: int 
     not given).  head_dim 128.  ``ctas`` / ``key_chunks`` override the work split (0 =
     automatic).  The scratch for the partial results of key chunks comes from ``workspace`` (a
     byte tensor of at least the bytes ``ps_attention_workspace`` reports) or is allocated.
+    ``check_timeouts=True`` synchronises the device after the launch and raises ``PrepError``
+    if a bounded wait of the kernel ran out since the last check (``out`` is then undefined);
+    without it, callers poll ``attention_timeouts``.
     """
     if q.dtype is not torch.bfloat16 or k.dtype is not torch.bfloat16 or v.dtype is not torch.bfloat16:
         raise PrepError("attention takes bfloat16 q, k and v")
@@ -661,6 +665,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_tokens: int 
         args.workspace_bytes = workspace.numel() * workspace.element_size()
         if Lq:
             _check(lib.ps_ring_attention(ctypes.byref(args), _stream(device)))
+    if check_timeouts:
+        count = attention_timeouts(reset=True, device=device.index)
+        if count:
+            raise PrepError(f"{count} bounded wait(s) of the attention kernel ran out on cuda:{device.index}: "
+                            "the outputs of the calls since the last check are undefined")
     return out
 
 

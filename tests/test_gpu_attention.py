@@ -122,3 +122,13 @@ def test_attention_rejects_bad_arguments():
         ops.attention(q, k, v, 33, heads=1)              # window beyond the rows
     with pytest.raises(ops.PrepError, match="128"):
         ops.attention(q, k, v, 32, heads=2)              # head_dim 64
+
+
+def test_attention_check_timeouts_passes_on_a_clean_call():
+    """``check_timeouts=True`` synchronises, finds no expired wait and returns the same output."""
+    heads, Lq, kv, rows = 4, 300, 700, 800
+    q, k, v = _inputs(1, Lq, rows, heads, seed=21)
+    plain = ops.attention(q, k, v, kv, heads=heads)
+    checked = ops.attention(q, k, v, kv, heads=heads, check_timeouts=True)
+    assert torch.equal(plain, checked)
+    assert ops.attention_timeouts(reset=True) == 0
