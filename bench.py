@@ -181,14 +181,112 @@ _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_
             0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
 
 
-class ClockSampler:
-    """Samples this rank's GPU SM clock, power and clock-event reasons with NVML in a thread:
-    once at start, every ``period_s``, once at stop.  A sample costs milliseconds of NVML time
-    and NVML calls contend with CUDA calls of every process on the host: at a 2 ms period,
-    8 ranks' samplers doubled the 8-GPU pipeline's tick (host enqueue time = the tick), so the
-    period is 50 ms and power is read on every fourth sample only."""
+def ClockSampler(device_index):
+    """The clock sampler of a timed region: in-process NVML on one GPU; with several ranks an
+    ``nvidia-smi`` process per rank.  With NVML loaded in each of 8 bench processes the 8-GPU
+    pipeline's tick measured 2.0-2.4 ms with the host's enqueue time equal to the tick, at any
+    sampling period; the same run without NVML in the bench processes ticked in 0.96 ms."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return _SmiClockSampler(device_index)
+    return _NvmlClockSampler(device_index)
 
-    def __init__(self, device_index, period_s=0.05):
+
+class _SmiClockSampler:
+    """SM clock, power and clock-event reasons of this rank's GPU from ``nvidia-smi -lms``
+    (a separate process, line-buffered through ``stdbuf`` where available; a reader thread
+    collects its lines).  Samples whose own timestamps fall from one period before ``start`` to
+    one period after ``stop`` are kept, so a region shorter than the period still has the
+    samples around it."""
+
+    QUERY = "timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active"
+
+    def __init__(self, device_index, period_ms=20):
+        import subprocess
+
+        self.period = period_ms / 1000.0
+        self.lines = []
+        self.ok = False
+        self._t0 = self._t1 = None
+        try:
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            import shutil
+
+            cmd = ["nvidia-smi", "-i", bus, f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                   "-lms", str(period_ms)]
+            if shutil.which("stdbuf"):
+                cmd = ["stdbuf", "-oL", *cmd]
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+                                         bufsize=1)
+            self._thread = threading.Thread(target=self._read, daemon=True)
+            self._thread.start()
+            deadline = time.monotonic() + 5.0   # until nvidia-smi prints its first sample
+            while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.ok = bool(self.lines)
+            if not self.ok:
+                self.error = "nvidia-smi printed no sample"
+        except Exception as exc:  # noqa: BLE001 - a host without nvidia-smi still runs the bench
+            self.error = repr(exc)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def start(self):
+        self._t0 = time.time()
+
+    @staticmethod
+    def _parse(line):
+        """(sample time [s since the epoch, or None], sm MHz, max MHz, watts or None, reasons mask)."""
+        import datetime
+
+        stamp, sm, sm_max, power, reasons = (x.strip() for x in line.split(","))
+        try:
+            when = datetime.datetime.strptime(stamp, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            when = None
+        watts = float(power) if power.replace(".", "", 1).isdigit() else None
+        return when, int(float(sm)), int(float(sm_max)), watts, int(reasons, 16)
+
+    def stop(self):
+        self._t1 = time.time()
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"nvidia-smi unavailable: {self.error}"]}
+        deadline = self._t1 + max(10 * self.period, 1.0)   # one sample after the region
+        while time.time() < deadline and not any(t >= self._t1 for t, _ in self.lines):
+            time.sleep(0.005)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=2)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        rows = []
+        for arrived, line in self.lines:
+            try:
+                when, *sample = self._parse(line)
+            except ValueError:
+                continue
+            t = arrived if when is None else when
+            if self._t0 - self.period <= t <= self._t1 + self.period:
+                rows.append(sample)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi sample around the region"]}
+        mask = 0
+        for r in rows:
+            mask |= r[3]
+        watts = [r[2] for r in rows if r[2] is not None]
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                "reasons": [name for bit, name in _REASONS.items() if mask & bit], "samples": len(rows),
+                "power_w_max": max(watts) if watts else None, "source": "nvidia-smi"}
+
+
+class _NvmlClockSampler:
+    """Samples this GPU's SM clock, power and clock-event reasons with NVML in a thread: once
+    at start, every ``period_s``, once at stop (power on every fourth sample; a sample costs
+    milliseconds of NVML time)."""
+
+    def __init__(self, device_index, period_s=0.02):
         self.period = period_s
         self.samples = []
         self.ok = False
